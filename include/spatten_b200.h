@@ -1,0 +1,164 @@
+/*
+ * spatten_b200.h -- C ABI of the SpAtten sparse-attention hot path on B200
+ * (sm_100a). Shared library: spatten_b200/lib/libspatten_b200.so
+ *
+ * Plain pointers, sizes and element strides only; every device pointer must
+ * live on the current CUDA device, and `stream` is a cudaStream_t (NULL = the
+ * legacy default stream). Calls are asynchronous on `stream` and allocate no
+ * memory; where a kernel needs scratch, the caller passes a workspace whose
+ * size the matching *_workspace_size() call returns.
+ *
+ * Every entry point returns SPATTEN_OK (0) or an error code; the message of
+ * the last error on the calling thread is available from
+ * spatten_last_error(). Invalid arguments are rejected before any launch.
+ *
+ * Reference interfaces replaced (paths within Merlin0224/SpAtten):
+ *   spatten_quant_q_int8 / spatten_quant_k_planes
+ *       the float K split `k_msb = key*0.8; k_lsb = key*0.2`
+ *       (spatten_bert_ultimate.py:184-185), made integer.
+ *   spatten_prog_attn
+ *       triton_progressive_qk(q, k_msb, k_lsb, v, threshold, sm_scale)
+ *       (spatten_bert_ultimate.py:103-122),
+ *       spatten_progressive_attention(q, k_msb, k_lsb, v, threshold=0.1)
+ *       (spatten_progressive_attention.py:82-102), and the attention core of
+ *       SpattenBertSelfAttention.forward: QK^T, mask, softmax, V prune, P.V,
+ *       head and token importance (spatten_bert.py:81-136).
+ *   spatten_topk_indices
+ *       torch.sort(torch.topk(x, k).indices) for the head and token cascade
+ *       (spatten_bert.py:123-128, 143-148).
+ *   spatten_gather_rows
+ *       torch.gather of hidden states / cumulative scores on the token axis
+ *       (module.py:53-54, 62-63) and torch.index_select of head rows of the
+ *       Q/K/V weights (module.py:22-28).
+ */
+#ifndef SPATTEN_B200_H
+#define SPATTEN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPATTEN_OK 0
+#define SPATTEN_ERR_INVALID 1     /* bad argument (shape, stride, pointer, dtype) */
+#define SPATTEN_ERR_CUDA 2        /* a CUDA runtime call or launch failed */
+#define SPATTEN_ERR_UNSUPPORTED 3 /* valid request outside what this build implements */
+
+#define SPATTEN_DTYPE_F16 0
+#define SPATTEN_DTYPE_BF16 1
+#define SPATTEN_DTYPE_F32 2
+
+#define SPATTEN_MODE_QUANT 0  /* int8 Q, 4-bit MSB/LSB K planes, row max-prob refetch */
+#define SPATTEN_MODE_DENSE 1  /* float Q/K (progressive quantisation off) */
+#define SPATTEN_MODE_COMPAT 2 /* float K planes with the reference's tile criterion */
+
+/* ABI version; bumped on any incompatible change of this header. */
+int spatten_abi_version(void);
+/* Message of the last failed call on this thread ("" if none). */
+const char* spatten_last_error(void);
+
+/*
+ * Per-row symmetric int8 quantisation of Q.
+ *   x      [Z, H, M, D] of `dtype`, element strides (sz, sh, sm), last dim contiguous
+ *   q8     [Z, H, M, D] int8, contiguous
+ *   scale  [Z, H, M] fp32, contiguous: scale = max|x| / 127, q8 = rint(x / scale)
+ * D must be a multiple of 32 and at most 256.
+ */
+int spatten_quant_q_int8(const void* x, int dtype, int Z, int H, int M, int D, int64_t sz,
+                         int64_t sh, int64_t sm, int8_t* q8, float* scale, void* stream);
+
+/*
+ * Per-row symmetric int8 quantisation of K, split into 4-bit planes.
+ *   x      [Z, H, N, D] of `dtype`, element strides (sz, sh, sn)
+ *   msb    [Z, H, N, D/2] uint8: k8 >> 4 (signed nibble), two per byte
+ *   lsb    [Z, H, N, D/2] uint8: k8 & 15 (unsigned nibble), two per byte
+ *   scale  [Z, H, N] fp32
+ * Byte p of a packed row holds dim p (low nibble) and dim p + D/2 (high).
+ */
+int spatten_quant_k_planes(const void* x, int dtype, int Z, int H, int N, int D, int64_t sz,
+                           int64_t sh, int64_t sn, uint8_t* msb, uint8_t* lsb, float* scale,
+                           void* stream);
+
+/* Arguments of spatten_prog_attn. Strides are in elements of the tensor's
+ * own type (bytes for the packed planes); the last dimension is contiguous. */
+typedef struct spatten_prog_attn_args {
+  int mode;  /* SPATTEN_MODE_* */
+  int dtype; /* element type of v and out (and of q / k for DENSE, COMPAT) */
+  int Z, H, Hkv, M, N, D; /* batch, query heads, kv heads (H % Hkv == 0), queries, keys, head dim */
+
+  const void* q; /* QUANT: int8 [Z,H,M,D]; else dtype */
+  int64_t q_sz, q_sh, q_sm;
+  const float* q_scale; /* QUANT: [Z,H,M] contiguous */
+
+  const void* k0; /* QUANT: msb plane; DENSE: k; COMPAT: k_msb */
+  const void* k1; /* QUANT: lsb plane; DENSE: unused; COMPAT: k_lsb */
+  int64_t k_sz, k_sh, k_sn; /* shared by k0 and k1 */
+  const float* k_scale;     /* QUANT: [Z,Hkv,N] contiguous */
+
+  const void* v;
+  int64_t v_sz, v_sh, v_sn;
+
+  void* out; /* [Z, H, M, D] by strides; head h goes to slot out_head_map[h] if given */
+  int64_t o_sz, o_sh, o_sm;
+  const int32_t* out_head_map; /* optional device array [H] of slots in [0, out_head_slots) */
+  int out_head_slots;          /* number of head slots of `out` (0 = H); a slot outside
+                                  [0, out_head_slots) is not written */
+
+  const float* bias; /* optional additive fp32 bias, element (z,h,m,n) at
+                        z*b_sz + h*b_sh + m*b_sm + n*b_sn (0 strides broadcast) */
+  int64_t b_sz, b_sh, b_sm, b_sn;
+
+  float sm_scale;
+  float refetch_thr; /* QUANT: refetch the LSB plane of a row when 1/l_msb < thr */
+  float v_thr;       /* V prune: p < v_thr -> 0 (0 disables) */
+  int tile_m, tile_n; /* COMPAT: criterion tile (32 or 64 each) */
+  float tile_thr;     /* COMPAT: refetch a tile when max(q.k_msb*sm_scale) < tile_thr */
+  int causal;         /* mask key n > m + (N - M) */
+
+  float* tok_out;      /* optional [Z, N]: sum over heads and queries of pruned P */
+  const float* tok_in; /* optional [Z, N]: added to tok_out (cumulative score) */
+  float* head_out;     /* optional [H]: sum over (z, m, d) of |out| */
+  uint8_t* refetch_out; /* optional QUANT [Z, H, M]: 1 where the row was refetched */
+  int32_t* score_out;   /* optional QUANT [Z, H, M, N]: the exact integer score each row used,
+                           q8.(16*msb) or, for a refetched row, q8.k8 (for verification) */
+} spatten_prog_attn_args;
+
+/* Bytes of workspace spatten_prog_attn needs for these arguments (0 if no
+ * importance output is requested). */
+size_t spatten_prog_attn_workspace_size(const spatten_prog_attn_args* a);
+
+/* Progressive sparse attention; see spatten_prog_attn_args. `workspace` must
+ * hold spatten_prog_attn_workspace_size(a) bytes (256-byte aligned). */
+int spatten_prog_attn(const spatten_prog_attn_args* a, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/*
+ * Top-k selection, indices returned in ascending order:
+ *   out[r, :] = sort(topk(x[r, :n], k).indices), r < rows
+ * Ties at the k-th value go to the smaller index. x fp32 with row stride
+ * `x_row_stride` (elements); out int64 [rows, k] contiguous.
+ */
+int spatten_topk_indices(const float* x, int rows, int n, int64_t x_row_stride, int k,
+                         int64_t* out, void* stream);
+
+/*
+ * Row gather (stream compaction):
+ *   dst[b, i*rows_per_idx + j, :] = src[b, idx[b, i] * idx_scale + j, :]
+ * for j < rows_per_idx, as raw bytes: row_bytes per row, strides in bytes
+ * (batch, row). src holds src_rows rows per batch; a source row outside
+ * [0, src_rows) zero-fills its destination row. idx int64 [B, K] with row
+ * stride idx_b_stride (0 = one index list shared by all batches).
+ */
+int spatten_gather_rows(const void* src, int64_t src_b_stride, int64_t src_r_stride,
+                        int64_t src_rows, const int64_t* idx, int64_t idx_b_stride, int B, int K,
+                        int rows_per_idx,
+                        int64_t idx_scale, int64_t row_bytes, void* dst, int64_t dst_b_stride,
+                        int64_t dst_r_stride, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPATTEN_B200_H */

@@ -1,0 +1,231 @@
+// extern "C" entry points of libspatten_b200.so (declared in include/spatten_b200.h).
+//
+// Every call validates its arguments on the host before any launch, records
+// a message for spatten_last_error() and returns an error code; nothing here
+// synchronises the stream or allocates device memory.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/spatten_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int ok() {
+  g_err.clear();
+  return SPATTEN_OK;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(SPATTEN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+int esize(int dtype) { return dtype == SPATTEN_DTYPE_F32 ? 4 : 2; }
+
+bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+bool smul(int64_t s, int64_t esz, int a) { return (s * esz) % a == 0; }
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+int check_quant_args(const void* x, int dtype, int Z, int H, int M, int D, int64_t s0,
+                     int64_t s1, int64_t s2) {
+  if (!x) return fail(SPATTEN_ERR_INVALID, "quant: null input");
+  if (dtype < 0 || dtype > 2) return fail(SPATTEN_ERR_INVALID, "quant: bad dtype %d", dtype);
+  if (Z < 0 || H < 0 || M < 0) return fail(SPATTEN_ERR_INVALID, "quant: negative shape");
+  if (!(D == 32 || D == 64 || D == 128 || D == 256))
+    return fail(SPATTEN_ERR_UNSUPPORTED, "quant: D=%d (need 32, 64, 128 or 256)", D);
+  if (s0 < 0 || s1 < 0 || s2 < 0) return fail(SPATTEN_ERR_INVALID, "quant: negative stride");
+  return SPATTEN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int spatten_abi_version(void) { return 1; }
+
+const char* spatten_last_error(void) { return g_err.c_str(); }
+
+int spatten_quant_q_int8(const void* x, int dtype, int Z, int H, int M, int D, int64_t sz,
+                         int64_t sh, int64_t sm, int8_t* q8, float* scale, void* stream) {
+  if (int e = check_quant_args(x, dtype, Z, H, M, D, sz, sh, sm)) return e;
+  if (!q8 || !scale) return fail(SPATTEN_ERR_INVALID, "quant_q_int8: null output");
+  if ((int64_t)Z * H * M == 0) return ok();
+  return cuda_status(spatten::launch_quant(dtype, false, x, Z, H, M, D, sz, sh, sm, q8, nullptr,
+                                           nullptr, scale, (cudaStream_t)stream, sm_count()),
+                     "quant_q_int8 launch");
+}
+
+int spatten_quant_k_planes(const void* x, int dtype, int Z, int H, int N, int D, int64_t sz,
+                           int64_t sh, int64_t sn, uint8_t* msb, uint8_t* lsb, float* scale,
+                           void* stream) {
+  if (int e = check_quant_args(x, dtype, Z, H, N, D, sz, sh, sn)) return e;
+  if (!msb || !lsb || !scale) return fail(SPATTEN_ERR_INVALID, "quant_k_planes: null output");
+  if ((int64_t)Z * H * N == 0) return ok();
+  return cuda_status(spatten::launch_quant(dtype, true, x, Z, H, N, D, sz, sh, sn, nullptr, msb,
+                                           lsb, scale, (cudaStream_t)stream, sm_count()),
+                     "quant_k_planes launch");
+}
+
+static int fill_params(const spatten_prog_attn_args* a, spatten::AttnParams& p) {
+  if (!a) return fail(SPATTEN_ERR_INVALID, "prog_attn: null args");
+  if (a->mode < 0 || a->mode > 2) return fail(SPATTEN_ERR_INVALID, "prog_attn: bad mode %d", a->mode);
+  if (a->dtype < 0 || a->dtype > 2) return fail(SPATTEN_ERR_INVALID, "prog_attn: bad dtype %d", a->dtype);
+  if (a->dtype == SPATTEN_DTYPE_F32)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: fp32 tensors are not supported (use f16/bf16)");
+  if (a->Z < 1 || a->H < 1 || a->Hkv < 1 || a->M < 1 || a->N < 1)
+    return fail(SPATTEN_ERR_INVALID, "prog_attn: empty shape Z=%d H=%d Hkv=%d M=%d N=%d", a->Z,
+                a->H, a->Hkv, a->M, a->N);
+  if (a->H % a->Hkv) return fail(SPATTEN_ERR_INVALID, "prog_attn: H %% Hkv != 0");
+  if (a->H > 65535 || a->Z > 65535) return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: Z or H > 65535");
+  if (a->D != 64 && a->D != 128) return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: D=%d (need 64 or 128)", a->D);
+  if (!a->q || !a->k0 || !a->v || !a->out) return fail(SPATTEN_ERR_INVALID, "prog_attn: null q/k/v/out");
+  const bool quant = a->mode == SPATTEN_MODE_QUANT;
+  if (quant && (!a->q_scale || !a->k1 || !a->k_scale))
+    return fail(SPATTEN_ERR_INVALID, "prog_attn: QUANT needs q_scale, lsb plane and k_scale");
+  if (a->mode == SPATTEN_MODE_COMPAT && !a->k1) return fail(SPATTEN_ERR_INVALID, "prog_attn: COMPAT needs k_lsb");
+  if (a->mode == SPATTEN_MODE_COMPAT &&
+      !((a->tile_m == 32 || a->tile_m == 64) && (a->tile_n == 32 || a->tile_n == 64)))
+    return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: COMPAT tile %dx%d (need 32/64)", a->tile_m, a->tile_n);
+  const int es = esize(a->dtype);
+  const int qes = quant ? 1 : es;
+  const int kes = quant ? 1 : es;
+  // q: 4-byte fragment loads
+  if (!aligned(a->q, 4) || !smul(a->q_sz, qes, 4) || !smul(a->q_sh, qes, 4) || !smul(a->q_sm, qes, 4))
+    return fail(SPATTEN_ERR_INVALID, "prog_attn: q pointer/strides not 4-byte aligned");
+  // k planes / k, v: 16-byte cp.async rows
+  if (!aligned(a->k0, 16) || (a->k1 && !aligned(a->k1, 16)) || !smul(a->k_sz, kes, 16) ||
+      !smul(a->k_sh, kes, 16) || !smul(a->k_sn, kes, 16))
+    return fail(SPATTEN_ERR_INVALID, "prog_attn: k pointer/strides not 16-byte aligned");
+  if (!aligned(a->v, 16) || !smul(a->v_sz, es, 16) || !smul(a->v_sh, es, 16) || !smul(a->v_sn, es, 16))
+    return fail(SPATTEN_ERR_INVALID, "prog_attn: v pointer/strides not 16-byte aligned");
+  if (!aligned(a->out, 4) || !smul(a->o_sz, es, 4) || !smul(a->o_sh, es, 4) || !smul(a->o_sm, es, 4))
+    return fail(SPATTEN_ERR_INVALID, "prog_attn: out pointer/strides not 4-byte aligned");
+  if (a->bias && !aligned(a->bias, 4)) return fail(SPATTEN_ERR_INVALID, "prog_attn: bias not aligned");
+  if (a->q_scale && !aligned(a->q_scale, 4)) return fail(SPATTEN_ERR_INVALID, "prog_attn: q_scale not aligned");
+  if (a->k_scale && !aligned(a->k_scale, 4)) return fail(SPATTEN_ERR_INVALID, "prog_attn: k_scale not aligned");
+  if (a->q_sz < 0 || a->q_sh < 0 || a->q_sm < 0 || a->k_sz < 0 || a->k_sh < 0 || a->k_sn < 0 ||
+      a->v_sz < 0 || a->v_sh < 0 || a->v_sn < 0 || a->o_sz < 0 || a->o_sh < 0 || a->o_sm < 0)
+    return fail(SPATTEN_ERR_INVALID, "prog_attn: negative stride");
+  if (a->tok_in && !a->tok_out) return fail(SPATTEN_ERR_INVALID, "prog_attn: tok_in without tok_out");
+  p.mode = a->mode;
+  p.dtype = a->dtype;
+  p.Z = a->Z; p.H = a->H; p.Hkv = a->Hkv; p.M = a->M; p.N = a->N; p.D = a->D;
+  p.q = a->q; p.q_sz = a->q_sz; p.q_sh = a->q_sh; p.q_sm = a->q_sm; p.q_scale = a->q_scale;
+  p.k0 = a->k0; p.k1 = a->k1; p.k_sz = a->k_sz; p.k_sh = a->k_sh; p.k_sn = a->k_sn;
+  p.k_scale = a->k_scale;
+  p.v = a->v; p.v_sz = a->v_sz; p.v_sh = a->v_sh; p.v_sn = a->v_sn;
+  p.out = a->out; p.o_sz = a->o_sz; p.o_sh = a->o_sh; p.o_sm = a->o_sm;
+  p.out_head_map = a->out_head_map;
+  p.out_head_slots = a->out_head_slots > 0 ? a->out_head_slots : a->H;
+  p.bias = a->bias; p.b_sz = a->b_sz; p.b_sh = a->b_sh; p.b_sm = a->b_sm; p.b_sn = a->b_sn;
+  p.sm_scale = a->sm_scale; p.refetch_thr = a->refetch_thr; p.v_thr = a->v_thr;
+  p.tile_m = a->tile_m; p.tile_n = a->tile_n; p.tile_thr = a->tile_thr;
+  p.causal = a->causal;
+  p.refetch_out = quant ? a->refetch_out : nullptr;
+  p.score_out = quant ? a->score_out : nullptr;
+  const int rows = spatten::attn_tile_rows(p);
+  p.mtiles = (a->M + rows - 1) / rows;
+  p.tok_partial = nullptr;
+  p.head_partial = nullptr;
+  return SPATTEN_OK;
+}
+
+static void workspace_layout(const spatten::AttnParams& p, bool tok, bool head, size_t& tok_bytes,
+                             size_t& head_bytes) {
+  tok_bytes = tok ? align256((size_t)p.Z * p.H * p.mtiles * p.N * sizeof(float)) : 0;
+  head_bytes = head ? align256((size_t)p.Z * p.H * p.mtiles * sizeof(float)) : 0;
+}
+
+size_t spatten_prog_attn_workspace_size(const spatten_prog_attn_args* a) {
+  spatten::AttnParams p;
+  if (fill_params(a, p) != SPATTEN_OK) return 0;
+  size_t tb, hb;
+  workspace_layout(p, a->tok_out != nullptr, a->head_out != nullptr, tb, hb);
+  return tb + hb;
+}
+
+int spatten_prog_attn(const spatten_prog_attn_args* a, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  spatten::AttnParams p;
+  if (int e = fill_params(a, p)) return e;
+  size_t tb, hb;
+  workspace_layout(p, a->tok_out != nullptr, a->head_out != nullptr, tb, hb);
+  if (tb + hb > 0) {
+    if (!workspace || workspace_bytes < tb + hb)
+      return fail(SPATTEN_ERR_INVALID, "prog_attn: workspace of %zu bytes needed, %zu given",
+                  tb + hb, workspace_bytes);
+    if (!aligned(workspace, 256)) return fail(SPATTEN_ERR_INVALID, "prog_attn: workspace not 256-byte aligned");
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    if (tb) p.tok_partial = reinterpret_cast<float*>(w);
+    if (hb) p.head_partial = reinterpret_cast<float*>(w + tb);
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = spatten::launch_prog_attn(p, st, sm_count());
+  if (e != cudaSuccess) return cuda_status(e, "prog_attn launch");
+  if (tb + hb > 0) {
+    e = spatten::launch_importance_reduce(p.tok_partial, p.head_partial, p.Z, p.H, p.mtiles, p.N,
+                                          a->tok_in, a->tok_out, a->head_out, st);
+    if (e != cudaSuccess) return cuda_status(e, "importance reduce launch");
+  }
+  return ok();
+}
+
+int spatten_topk_indices(const float* x, int rows, int n, int64_t x_row_stride, int k,
+                         int64_t* out, void* stream) {
+  if (!x || !out) return fail(SPATTEN_ERR_INVALID, "topk: null pointer");
+  if (rows < 0 || n < 1 || k < 1 || k > n)
+    return fail(SPATTEN_ERR_INVALID, "topk: need rows >= 0, 1 <= k <= n (rows=%d n=%d k=%d)", rows, n, k);
+  if (rows > 0 && x_row_stride < n) return fail(SPATTEN_ERR_INVALID, "topk: row stride < n");
+  if (rows == 0) return ok();
+  return cuda_status(spatten::launch_topk(x, rows, n, x_row_stride, k, out, (cudaStream_t)stream),
+                     "topk launch");
+}
+
+int spatten_gather_rows(const void* src, int64_t src_b_stride, int64_t src_r_stride,
+                        int64_t src_rows, const int64_t* idx, int64_t idx_b_stride, int B, int K,
+                        int rows_per_idx, int64_t idx_scale, int64_t row_bytes, void* dst,
+                        int64_t dst_b_stride, int64_t dst_r_stride, void* stream) {
+  if (!src || !idx || !dst) return fail(SPATTEN_ERR_INVALID, "gather: null pointer");
+  if (B < 0 || K < 0 || rows_per_idx < 1 || row_bytes < 1 || src_rows < 0)
+    return fail(SPATTEN_ERR_INVALID, "gather: bad sizes");
+  if (src_b_stride < 0 || src_r_stride < 0 || dst_b_stride < 0 || dst_r_stride < 0 || idx_b_stride < 0)
+    return fail(SPATTEN_ERR_INVALID, "gather: negative stride");
+  if ((int64_t)B * K == 0) return ok();
+  return cuda_status(spatten::launch_gather(src, src_b_stride, src_r_stride, idx, idx_b_stride, B,
+                                            K, rows_per_idx, idx_scale, row_bytes, dst,
+                                            dst_b_stride, dst_r_stride, (cudaStream_t)stream,
+                                            sm_count(), src_rows),
+                     "gather launch");
+}
+
+}  // extern "C"

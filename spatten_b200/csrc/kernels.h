@@ -1,0 +1,59 @@
+// Internal launcher declarations (host side) shared by the C-ABI layer.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace spatten {
+
+// Device-side view of spatten_prog_attn_args plus the workspace layout.
+struct AttnParams {
+  int mode, dtype;
+  int Z, H, Hkv, M, N, D;
+  const void* q;
+  int64_t q_sz, q_sh, q_sm;
+  const float* q_scale;
+  const void* k0;
+  const void* k1;
+  int64_t k_sz, k_sh, k_sn;
+  const float* k_scale;
+  const void* v;
+  int64_t v_sz, v_sh, v_sn;
+  void* out;
+  int64_t o_sz, o_sh, o_sm;
+  const int32_t* out_head_map;
+  int out_head_slots;
+  const float* bias;
+  int64_t b_sz, b_sh, b_sm, b_sn;
+  float sm_scale, refetch_thr, v_thr;
+  int tile_m, tile_n;
+  float tile_thr;
+  int causal;
+  uint8_t* refetch_out;
+  int32_t* score_out;
+  // workspace (per-CTA partial sums, reduced by importance_reduce)
+  int mtiles;           // query tiles per (z, h)
+  float* tok_partial;   // [Z, H, mtiles, N] or null
+  float* head_partial;  // [Z, H, mtiles] or null
+};
+
+cudaError_t launch_quant(int dtype, bool planes, const void* x, int Z, int H, int M, int D,
+                         int64_t sz, int64_t sh, int64_t sm, int8_t* q8, uint8_t* msb,
+                         uint8_t* lsb, float* scale, cudaStream_t st, int n_sm);
+
+// Rows of queries per CTA of the attention kernel (granularity of partials).
+int attn_tile_rows(const AttnParams& p);
+cudaError_t launch_prog_attn(const AttnParams& p, cudaStream_t st, int n_sm);
+
+cudaError_t launch_importance_reduce(const float* tok_partial, const float* head_partial, int Z,
+                                     int H, int mtiles, int N, const float* tok_in,
+                                     float* tok_out, float* head_out, cudaStream_t st);
+
+cudaError_t launch_topk(const float* x, int rows, int n, int64_t row_stride, int k,
+                        int64_t* out, cudaStream_t st);
+
+cudaError_t launch_gather(const void* src, int64_t src_b, int64_t src_r, const int64_t* idx,
+                          int64_t idx_b, int B, int K, int rows_per_idx, int64_t idx_scale,
+                          int64_t row_bytes, void* dst, int64_t dst_b, int64_t dst_r,
+                          cudaStream_t st, int n_sm, int64_t src_rows);
+
+}  // namespace spatten

@@ -1,0 +1,126 @@
+"""The C-ABI library loads, exports every symbol include/*.h declares, and
+rejects invalid arguments on the host (no GPU needed: nothing here launches)."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from tests.conftest import ROOT
+
+
+def _declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\*?\s*(spatten_[a-z_0-9]+)\s*\(",
+                             src, flags=re.M):
+            names.add(m.group(1))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = _declared_symbols()
+    for n in ("spatten_prog_attn", "spatten_quant_k_planes", "spatten_quant_q_int8",
+              "spatten_topk_indices", "spatten_gather_rows", "spatten_last_error",
+              "spatten_abi_version", "spatten_prog_attn_workspace_size"):
+        assert n in names, n
+
+
+def test_library_exports_every_declared_symbol():
+    from spatten_b200 import _native as N
+    lib = ctypes.CDLL(N.LIB_PATH)
+    missing = [n for n in _declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+    # the Python bindings cover the whole header
+    assert _declared_symbols() <= set(N.SIGNATURES)
+
+
+def test_abi_version():
+    from spatten_b200 import _native as N
+    assert N.lib.spatten_abi_version() == N.ABI_VERSION
+
+
+def _args(lib_mod, **kw):
+    N = lib_mod
+    a = N.ProgAttnArgs()
+    a.mode, a.dtype = N.MODE_QUANT, N.DTYPE_F16
+    a.Z, a.H, a.Hkv, a.M, a.N, a.D = 2, 4, 4, 100, 257, 64
+    a.q = a.k0 = a.k1 = a.v = a.out = 1 << 20
+    a.q_scale = a.k_scale = 1 << 20
+    a.q_sz, a.q_sh, a.q_sm = 4 * 100 * 64, 100 * 64, 64
+    a.k_sz, a.k_sh, a.k_sn = 4 * 257 * 32, 257 * 32, 32
+    a.v_sz, a.v_sh, a.v_sn = 4 * 257 * 64, 257 * 64, 64
+    a.o_sz, a.o_sh, a.o_sm = 4 * 100 * 64, 100 * 64, 64
+    a.sm_scale, a.refetch_thr = 0.125, 0.1
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def test_workspace_size_matches_partials():
+    from spatten_b200 import _native as N
+    a = _args(N)
+    assert N.lib.spatten_prog_attn_workspace_size(a) == 0
+    a.tok_out = 1 << 21
+    a.head_out = 1 << 22
+    ws = N.lib.spatten_prog_attn_workspace_size(a)
+    mtiles = (100 + 63) // 64
+    tok = 2 * 4 * mtiles * 257 * 4
+    head = 2 * 4 * mtiles * 4
+    r = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    assert ws == r(tok) + r(head)
+
+
+@pytest.mark.parametrize("field,value,code", [
+    ("mode", 7, 1), ("dtype", 9, 1), ("dtype", 2, 3), ("D", 96, 3), ("M", 0, 1), ("N", 0, 1),
+    ("Hkv", 3, 1), ("q", 0, 1), ("k1", 0, 1), ("k0", (1 << 20) + 8, 1), ("v_sn", 65, 1),
+    ("q_sm", -64, 1),
+])
+def test_prog_attn_rejects_bad_args(field, value, code):
+    from spatten_b200 import _native as N
+    a = _args(N, **{field: value})
+    rc = N.lib.spatten_prog_attn(a, None, 0, None)
+    assert rc == code
+    assert N.lib.spatten_last_error().decode()
+
+
+def test_prog_attn_requires_workspace():
+    from spatten_b200 import _native as N
+    a = _args(N, tok_out=1 << 21)
+    assert N.lib.spatten_prog_attn(a, None, 0, None) == N.ERR_INVALID
+    assert b"workspace" in N.lib.spatten_last_error()
+
+
+def test_compat_tile_validation():
+    from spatten_b200 import _native as N
+    a = _args(N, mode=N.MODE_COMPAT, tile_m=16, tile_n=32)
+    a.k_sn = 64
+    assert N.lib.spatten_prog_attn(a, None, 0, None) == N.ERR_UNSUPPORTED
+
+
+def test_topk_gather_quant_reject_bad_args():
+    from spatten_b200 import _native as N
+    L = N.lib
+    assert L.spatten_topk_indices(None, 1, 4, 4, 2, None, None) == N.ERR_INVALID
+    assert L.spatten_topk_indices(1 << 20, 1, 4, 4, 5, 1 << 21, None) == N.ERR_INVALID
+    assert L.spatten_topk_indices(1 << 20, 2, 4, 3, 2, 1 << 21, None) == N.ERR_INVALID
+    assert L.spatten_gather_rows(None, 0, 0, 1, None, 0, 1, 1, 1, 1, 4, None, 0, 0, None) == N.ERR_INVALID
+    assert L.spatten_gather_rows(1 << 20, 0, 4, 1, 1 << 21, 0, 1, 1, 0, 1, 4, 1 << 22, 0, 4, None) == N.ERR_INVALID
+    assert L.spatten_quant_q_int8(1 << 20, 0, 1, 1, 1, 48, 0, 0, 48, 1 << 21, 1 << 22, None) == N.ERR_UNSUPPORTED
+    assert L.spatten_quant_k_planes(None, 0, 1, 1, 1, 64, 0, 0, 64, 1, 1, 1, None) == N.ERR_INVALID
+    # empty work is a no-op that succeeds without touching the device
+    assert L.spatten_topk_indices(1 << 20, 0, 4, 4, 2, 1 << 21, None) == N.OK
+    assert L.spatten_gather_rows(1 << 20, 0, 4, 1, 1 << 21, 0, 0, 1, 1, 1, 4, 1 << 22, 0, 4, None) == N.OK
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    import spatten_b200 as sp
+    x = torch.zeros(1, 1, 4, 64, dtype=torch.float16)
+    with pytest.raises(ValueError, match="no CPU path"):
+        sp.quant_q_int8(x)
+    with pytest.raises(ValueError, match="no CPU path"):
+        sp.topk_indices(torch.zeros(4), 2)
