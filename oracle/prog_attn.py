@@ -84,7 +84,7 @@ def _finish(p, vv, v_thr):
 
 
 def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.0,
-                    bias=None, causal=False, return_scores=False):
+                    bias=None, causal=False, return_scores=False, band=1e-4):
     """Integer progressive attention. Shapes: q8 [Z,H,M,D] int8, sq [Z,H,M],
     msb_p/lsb_p [Z,Hkv,N,D/2] uint8 (packed, see oracle.quant), sk [Z,Hkv,N],
     v [Z,Hkv,N,D]. Returns a dict of float64 outputs and diagnostics."""
@@ -97,6 +97,7 @@ def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.
     maxprob = np.zeros((Z, H, M))
     tok_h = np.zeros((Z, H, N))
     head_abs = np.zeros((Z, H))
+    amb = np.zeros((Z, N))
     pgap = np.inf
     scores = {}
     excl = _causal_mask(M, N) if causal else None
@@ -125,6 +126,7 @@ def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.
             if v_thr > 0:
                 gap = np.min(np.abs(p - v_thr)) / v_thr
                 pgap = min(pgap, gap)
+                amb[z] += (np.abs(p - v_thr) < band * v_thr).sum(axis=0)
             pp, o = _finish(p, np.asarray(v[z, kh]), v_thr)
             out[z, h] = o
             refetch[z, h] = rf
@@ -134,14 +136,14 @@ def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.
             if return_scores:
                 scores[(z, h)] = (A, F)
     res = dict(out=out, refetch=refetch, maxprob_msb=maxprob, tok_per_head=tok_h,
-               tok=tok_h.sum(axis=1), head_abs=head_abs, vprune_gap=pgap,
+               tok=tok_h.sum(axis=1), head_abs=head_abs, vprune_gap=pgap, vprune_amb=amb,
                refetch_gap=np.min(np.abs(maxprob - refetch_thr)) / max(abs(refetch_thr), 1e-30))
     if return_scores:
         res["scores"] = scores
     return res
 
 
-def prog_attn_dense(q, k, v, sm_scale, v_thr=0.0, bias=None, causal=False):
+def prog_attn_dense(q, k, v, sm_scale, v_thr=0.0, bias=None, causal=False, band=1e-4):
     """Float attention with V pruning and importance (progressive quant off).
     Scores: fp32(q) . fp32(k) * sm_scale + bias, evaluated in float64 then
     rounded to fp32."""
@@ -151,6 +153,7 @@ def prog_attn_dense(q, k, v, sm_scale, v_thr=0.0, bias=None, causal=False):
     out = np.zeros((Z, H, M, D))
     tok_h = np.zeros((Z, H, N))
     head_abs = np.zeros((Z, H))
+    amb = np.zeros((Z, N))
     pgap = np.inf
     excl = _causal_mask(M, N) if causal else None
     for z in range(Z):
@@ -164,12 +167,13 @@ def prog_attn_dense(q, k, v, sm_scale, v_thr=0.0, bias=None, causal=False):
             p, _, _ = _softmax_rows(s, excl)
             if v_thr > 0:
                 pgap = min(pgap, np.min(np.abs(p - v_thr)) / v_thr)
+                amb[z] += (np.abs(p - v_thr) < band * v_thr).sum(axis=0)
             pp, o = _finish(p, np.asarray(v[z, kh]), v_thr)
             out[z, h] = o
             tok_h[z, h] = pp.sum(axis=0)
             head_abs[z, h] = np.abs(o).sum()
     return dict(out=out, tok_per_head=tok_h, tok=tok_h.sum(axis=1), head_abs=head_abs,
-                vprune_gap=pgap)
+                vprune_gap=pgap, vprune_amb=amb)
 
 
 def prog_attn_compat(q, k_msb, k_lsb, v, threshold, sm_scale, bm=32, bn=32):

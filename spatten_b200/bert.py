@@ -1,0 +1,233 @@
+"""Drop-in SpAtten cascade for Hugging Face BERT, running on the C-ABI kernels.
+
+Same API as the reference:
+
+* ``SpattenBertSelfAttention(config)`` -- subclass of HF ``BertSelfAttention``
+  with the reference's knobs and cascade attributes
+  (spatten_bert.py:15-37, spatten_bert_ultimate.py:128-152), loadable with
+  ``load_state_dict(orig.state_dict())``; ``forward(hidden, attention_mask)``
+  returns ``(context [B, S, hidden], None)``.
+* ``spatten_encoder_forward(self, hidden_states, attention_mask=None, **kw)``
+  -- the cascade encoder loop (module.py:40-99), bound with
+  ``encoder.forward = spatten_encoder_forward.__get__(encoder, BertEncoder)``.
+* ``slice_linear_weights(linear, active_indices, num_heads, head_dim)``
+  (module.py:12-34), on the device gather kernel.
+* ``patch_bert(model)`` does the module swap and the binding in one call.
+
+Knobs (per attention module): ``enable_head_prune``/``head_prune_num``,
+``enable_token_prune``/``token_prune_num``, ``enable_v_prune``/``v_prune_num``,
+``enable_prog_quant``/``quant_threshold`` as in the reference, plus the ratio
+and threshold knobs ``head_keep_ratio``, ``token_keep_ratio`` (keep
+``max(1, ceil(ratio * current))``, overriding the count) and
+``v_prune_threshold`` (zero ``p < thr``; used instead of the count when set).
+``quant_threshold`` is the row max-probability below which a row's LSB plane
+is refetched (the reference used it as a tile logit bound).
+
+On CUDA every step runs through libspatten_b200: head-row weight gather, one
+cuBLAS GEMM for the selected Q/K/V rows, int8/4-bit quantisation, the fused
+attention (mask, softmax, V prune, P.V, importance, scatter into the
+full-width context), and the radix-select top-k for heads and tokens. There is
+no CPU path: a CPU module raises.
+"""
+import math
+from fractions import Fraction
+
+import torch
+import torch.nn.functional as F
+from transformers.modeling_outputs import BaseModelOutputWithPastAndCrossAttentions
+from transformers.models.bert.modeling_bert import BertEncoder, BertSelfAttention
+
+from . import _native as N
+from .progressive import prog_attn, quant_k_planes, quant_q_int8
+from .select import gather_head_rows, gather_rows, topk_indices
+
+
+def keep_count(ratio, current):
+    """``max(1, ceil(ratio * current))``, exact on the ratio's decimal repr."""
+    r = Fraction(repr(float(ratio)))
+    return max(1, math.ceil(r * current))
+
+
+def slice_linear_weights(linear_layer, active_indices, num_heads, head_dim):
+    """Rows of the active heads of a Linear (module.py:12-34): (W [h*d, in], b [h*d])."""
+    w = linear_layer.weight
+    b = linear_layer.bias
+    if not w.is_cuda:
+        raise ValueError("slice_linear_weights: CUDA module expected (no CPU path)")
+    return gather_head_rows(w, active_indices, head_dim), gather_head_rows(b, active_indices, head_dim)
+
+
+def _mask_bias(attention_mask, B, S):
+    """HF mask as passed to the attention module -> additive bias view, or None.
+    Float masks are additive (eager); bool masks mark kept keys (sdpa)."""
+    if attention_mask is None:
+        return None
+    m = attention_mask
+    if m.dim() == 2:            # [B, S] 0/1 padding mask
+        m = m[:, None, None, :].to(torch.bool) if m.dtype != torch.bool else m[:, None, None, :]
+    if m.dim() == 3:
+        m = m[:, None]
+    if m.dtype == torch.bool:
+        return torch.zeros(m.shape, dtype=torch.float32, device=m.device).masked_fill_(
+            ~m, torch.finfo(torch.float32).min)
+    return m.float()
+
+
+class SpattenBertSelfAttention(BertSelfAttention):
+    """HF BertSelfAttention with the SpAtten cascade, on the B200 kernels."""
+
+    def __init__(self, config, *args, **kwargs):
+        super().__init__(config, *args, **kwargs)
+        self.layer_id = 0
+        self.num_heads = config.num_attention_heads
+        self.head_dim = int(config.hidden_size // config.num_attention_heads)
+        # reference knobs
+        self.head_prune_num = 0
+        self.enable_head_prune = False
+        self.next_active_head_indices = None
+        self.active_head_indices_for_this_layer = None
+        self.enable_token_prune = False
+        self.token_prune_num = 0
+        self.cumulative_token_score = None
+        self.next_active_token_indices = None
+        self.enable_v_prune = False
+        self.v_prune_num = 2
+        self.enable_prog_quant = False
+        self.quant_threshold = 1.0
+        # ratio / threshold knobs
+        self.head_keep_ratio = None
+        self.token_keep_ratio = None
+        self.v_prune_threshold = None
+        # diagnostics of the last forward
+        self.last_refetch = None
+        self.last_head_importance = None
+        self._qkv_cache = None
+
+    def _qkv_params(self):
+        key = tuple((p.data_ptr(), p._version) for p in (
+            self.query.weight, self.key.weight, self.value.weight,
+            self.query.bias, self.key.bias, self.value.bias))
+        if self._qkv_cache is None or self._qkv_cache[0] != key:
+            w = torch.cat([self.query.weight, self.key.weight, self.value.weight], 0).detach()
+            b = torch.cat([self.query.bias, self.key.bias, self.value.bias], 0).detach()
+            self._qkv_cache = (key, w, b)
+        return self._qkv_cache[1], self._qkv_cache[2]
+
+    def _prune_counts(self, cur_heads, seq_len):
+        hp = self.head_prune_num
+        if self.head_keep_ratio is not None:
+            hp = cur_heads - keep_count(self.head_keep_ratio, cur_heads)
+        tp = self.token_prune_num
+        if self.token_keep_ratio is not None:
+            tp = seq_len - keep_count(self.token_keep_ratio, seq_len)
+        return hp, tp
+
+    @torch.no_grad()
+    def forward(self, hidden_states, attention_mask=None, **kwargs):
+        if not hidden_states.is_cuda:
+            raise ValueError("SpattenBertSelfAttention runs on the CUDA kernels only")
+        dev = hidden_states.device
+        B, S, _ = hidden_states.shape
+        H, d = self.num_heads, self.head_dim
+        heads = self.active_head_indices_for_this_layer
+        if heads is None:
+            heads = torch.arange(H, device=dev)
+        cur = heads.numel()
+        # head-row gather of the concatenated Q/K/V weights, one GEMM
+        w, b = self._qkv_params()
+        rows = torch.cat([heads, heads + H, heads + 2 * H])
+        wsel = gather_head_rows(w, rows, d)
+        bsel = gather_head_rows(b, rows, d)
+        qkv = F.linear(hidden_states, wsel, bsel)          # [B, S, 3*cur*d]
+        qkv4 = qkv.view(B, S, 3, cur, d)
+        q = qkv4[:, :, 0].permute(0, 2, 1, 3)              # [B, cur, S, d] strided views
+        k = qkv4[:, :, 1].permute(0, 2, 1, 3)
+        v = qkv4[:, :, 2].permute(0, 2, 1, 3)
+        bias = _mask_bias(attention_mask, B, S)
+        v_thr = 0.0
+        if self.enable_v_prune:
+            if self.v_prune_threshold is not None:
+                v_thr = float(self.v_prune_threshold)
+            elif self.v_prune_num > 0 and S > self.v_prune_num:
+                raise NotImplementedError(
+                    "count-based V pruning (v_prune_num) is not implemented on the B200 path; "
+                    "set v_prune_threshold")
+        full = torch.zeros(B, S, H, d, dtype=hidden_states.dtype, device=dev)
+        cum = self.cumulative_token_score
+        common = dict(sm_scale=1.0 / math.sqrt(d), v_thr=v_thr, bias=bias, tok_in=cum,
+                      want_tok=True, want_head=True, out=full.permute(0, 2, 1, 3),
+                      out_head_map=heads, out_head_slots=H)
+        if self.enable_prog_quant:
+            q8, qs = quant_q_int8(q)
+            kp = quant_k_planes(k)
+            r = prog_attn(q8, kp.msb, v, k1=kp.lsb, mode=N.MODE_QUANT, q_scale=qs,
+                          k_scale=kp.scale, refetch_thr=float(self.quant_threshold),
+                          want_refetch=True, **common)
+            self.last_refetch = r.refetch
+        else:
+            r = prog_attn(q, k, v, mode=N.MODE_DENSE, **common)
+        head_imp = r.head_abs_sum / float(B * S * d)
+        self.last_head_importance = head_imp
+        hp, tp = self._prune_counts(cur, S)
+        next_heads = heads
+        if self.enable_head_prune and cur > hp:
+            keep = max(1, cur - hp)
+            pos = topk_indices(head_imp, keep)
+            next_heads = heads[pos]
+        self.next_active_head_indices = next_heads
+        self.cumulative_token_score = r.token_importance
+        next_tokens = None
+        if self.enable_token_prune and S > tp:
+            keep = max(1, S - tp)
+            next_tokens = topk_indices(self.cumulative_token_score, keep)
+        self.next_active_token_indices = next_tokens
+        return (full.view(B, S, H * d), None)
+
+
+def spatten_encoder_forward(self, hidden_states, attention_mask=None, **kwargs):
+    """Cascade encoder loop (module.py:40-99): per layer, compact the kept
+    tokens' hidden states, key mask and cumulative score, hand the active
+    heads and the score to the attention module, run the layer, and read its
+    decisions back."""
+    active_heads = None
+    active_tokens = None
+    cumulative = None
+    for layer in self.layer:
+        if active_tokens is not None:
+            hidden_states = gather_rows(hidden_states, active_tokens)
+            if attention_mask is not None:
+                m = attention_mask
+                if m.dim() == 4:      # [B, 1, Sq, Sk] -> key mask of query row 0, [B, 1, 1, K]
+                    m = m[:, :, :1, :]
+                attention_mask = gather_rows(m.reshape(m.shape[0], -1).unsqueeze(-1),
+                                             active_tokens).reshape(m.shape[0], 1, 1, -1)
+            if cumulative is not None:
+                cumulative = gather_rows(cumulative, active_tokens)
+        attn = layer.attention.self
+        attn.active_head_indices_for_this_layer = active_heads
+        attn.cumulative_token_score = cumulative
+        out = layer(hidden_states, attention_mask=attention_mask, **kwargs)
+        hidden_states = out[0] if isinstance(out, (tuple, list)) else out
+        active_heads = attn.next_active_head_indices
+        active_tokens = attn.next_active_token_indices
+        cumulative = attn.cumulative_token_score
+    return BaseModelOutputWithPastAndCrossAttentions(
+        last_hidden_state=hidden_states, past_key_values=None, hidden_states=None,
+        attentions=None, cross_attentions=None)
+
+
+def patch_bert(model, **knobs):
+    """Swap every layer's self-attention for SpattenBertSelfAttention (weights
+    carried over with load_state_dict, spatten_bert_ultimate.py:294-298),
+    bind the cascade encoder loop (:300) and set ``knobs`` on every layer."""
+    for i, layer in enumerate(model.encoder.layer):
+        old = layer.attention.self
+        new = SpattenBertSelfAttention(model.config)
+        new.load_state_dict(old.state_dict())
+        new.layer_id = i
+        new.to(device=old.query.weight.device, dtype=old.query.weight.dtype)
+        for k, v in knobs.items():
+            setattr(new, k, v)
+        layer.attention.self = new
+    model.encoder.forward = spatten_encoder_forward.__get__(model.encoder, BertEncoder)
+    return model
