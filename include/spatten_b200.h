@@ -58,6 +58,10 @@ extern "C" {
 int spatten_abi_version(void);
 /* Message of the last failed call on this thread ("" if none). */
 const char* spatten_last_error(void);
+/* Device error word of the current device (synchronous; 0 = none). A kernel
+ * whose bounded wait on a pipeline barrier runs out records a non-zero code
+ * here and returns instead of hanging; `reset` clears the word. */
+int spatten_device_error(unsigned int* code, int reset);
 
 /*
  * Per-row symmetric int8 quantisation of Q.

@@ -49,6 +49,7 @@ class ProgAttnArgs(ctypes.Structure):
 SIGNATURES = {
     "spatten_abi_version": (c_int, []),
     "spatten_last_error": (ctypes.c_char_p, []),
+    "spatten_device_error": (c_int, [ctypes.POINTER(ctypes.c_uint), c_int]),
     "spatten_quant_q_int8": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_int, c_i64, c_i64, c_i64,
                                      c_vp, c_vp, c_vp]),
     "spatten_quant_k_planes": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_int, c_i64, c_i64,
@@ -70,7 +71,7 @@ class SpattenError(RuntimeError):
 def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m spatten_b200.build` "
+            f"{LIB_PATH} is missing: build it with `python spatten_b200/build.py` "
             "(the CUDA library is the only compute path)")
     lib = ctypes.CDLL(LIB_PATH)
     for name, (res, args) in SIGNATURES.items():

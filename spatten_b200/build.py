@@ -1,6 +1,6 @@
 """Build libspatten_b200.so (the C-ABI library) for sm_100a with nvcc.
 
-    python -m spatten_b200.build [--force] [--verbose]
+    python spatten_b200/build.py [--force] [--verbose] [--ptxas]
 
 Each ``csrc/*.cu`` compiles to an object under ``spatten_b200/_build`` (in
 parallel), then the objects link into ``spatten_b200/lib/libspatten_b200.so``

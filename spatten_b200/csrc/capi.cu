@@ -75,6 +75,11 @@ int spatten_abi_version(void) { return 1; }
 
 const char* spatten_last_error(void) { return g_err.c_str(); }
 
+int spatten_device_error(unsigned int* code, int reset) {
+  if (!code) return fail(SPATTEN_ERR_INVALID, "device_error: null output");
+  return cuda_status(spatten::read_device_error(code, reset != 0), "device_error read");
+}
+
 int spatten_quant_q_int8(const void* x, int dtype, int Z, int H, int M, int D, int64_t sz,
                          int64_t sh, int64_t sm, int8_t* q8, float* scale, void* stream) {
   if (int e = check_quant_args(x, dtype, Z, H, M, D, sz, sh, sm)) return e;

@@ -43,6 +43,13 @@ cudaError_t launch_quant(int dtype, bool planes, const void* x, int Z, int H, in
 // Rows of queries per CTA of the attention kernel (granularity of partials).
 int attn_tile_rows(const AttnParams& p);
 cudaError_t launch_prog_attn(const AttnParams& p, cudaStream_t st, int n_sm);
+// tcgen05 kernel (QUANT and DENSE modes)
+int tc_tile_rows();
+cudaError_t launch_prog_attn_tc(const AttnParams& p, cudaStream_t st);
+// mma.sync kernel (COMPAT mode)
+cudaError_t launch_prog_attn_mma(const AttnParams& p, cudaStream_t st);
+// device error word written by a kernel whose bounded wait ran out
+cudaError_t read_device_error(unsigned int* code, bool reset);
 
 cudaError_t launch_importance_reduce(const float* tok_partial, const float* head_partial, int Z,
                                      int H, int mtiles, int N, const float* tok_in,

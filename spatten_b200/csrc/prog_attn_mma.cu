@@ -640,12 +640,19 @@ cudaError_t launch_m(const AttnParams& p, cudaStream_t st) {
 
 }  // namespace
 
-int attn_tile_rows(const AttnParams&) { return BM; }
-
-cudaError_t launch_prog_attn(const AttnParams& p, cudaStream_t st, int) {
+cudaError_t launch_prog_attn_mma(const AttnParams& p, cudaStream_t st) {
   if (p.dtype == kF16) return launch_m<__half>(p, st);
   if (p.dtype == kBF16) return launch_m<__nv_bfloat16>(p, st);
   return cudaErrorInvalidValue;
+}
+
+// QUANT and DENSE run on the tcgen05 kernel; the reference-compatible float
+// planes (COMPAT) on the warp-level kernel above.
+int attn_tile_rows(const AttnParams& p) { return p.mode == kCompat ? BM : tc_tile_rows(); }
+
+cudaError_t launch_prog_attn(const AttnParams& p, cudaStream_t st, int) {
+  if (p.mode == kCompat) return launch_prog_attn_mma(p, st);
+  return launch_prog_attn_tc(p, st);
 }
 
 }  // namespace spatten

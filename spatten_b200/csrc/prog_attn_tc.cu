@@ -1,0 +1,865 @@
+// Progressive sparse attention on the 5th-generation tensor cores (tcgen05).
+//
+// One CTA = 128 query rows of one (z, h), 8 warps, two CTAs per SM:
+//   warps 0-3  softmax: one query row per thread (TMEM lane = row). Reads S
+//              from TMEM, keeps the row statistics, decides the refetch,
+//              writes P (fp16/bf16) to shared memory, sums P's columns
+//              (token importance) and, at the end, reads O from TMEM.
+//   warp 4     TMA producer: 4-bit K planes (QUANT) or K (DENSE) and V tiles
+//              of 64 keys, straight into 128B-swizzled shared memory.
+//   warp 5     MMA issuer (one thread) and TMEM owner:
+//              S = Q' K'^T  (kind::i8, int32 accumulator, or kind::f16)
+//              O += P V     (kind::f16, fp32 accumulator, V MN-major)
+//   warps 6-7  expander (QUANT): one key per thread, unpacks the packed
+//              MSB/LSB nibbles into the int8 operand K' = [16*msb | lsb] and
+//              stages the per-key scale and mask bias for the softmax warps.
+// Tensor memory: two S buffers of 64 columns (int32 / fp32) and O (D fp32
+// columns). Every hand-off is an mbarrier; every wait is bounded (a timeout
+// records an error word and unwinds instead of hanging).
+//
+// Passes over K (the integer scores are exact; what follows them is fp32):
+//   pass 1   S = q8 . (16*msb)                     -> row max m, sum l
+//   decide   refetch = 1/l < refetch_thr (the row's max probability)
+//            Q' = [q8 | refetch ? q8 : 0]
+//   pass 1b  (only if a row of the CTA refetches; only then are LSB planes
+//            loaded) S = Q'.K' = q8.k8 for refetched rows -> their (m, l)
+//   pass 2   S = Q'.K'; P = exp(S - m)/l; P' = P < v_thr ? 0 : P;
+//            O += P'V; column sums of P' -> token-importance partials.
+// DENSE runs pass 1 and pass 2 with S = q.k (fp16/bf16 operands).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace spatten {
+
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;        // query rows per CTA (= TMEM lanes)
+constexpr int BN = 64;         // keys per tile
+constexpr int kThreads = 256;  // 8 warps
+constexpr int kNStg = 3;       // packed-plane staging stages (QUANT)
+constexpr int kNExp = 2;       // K operand stages
+constexpr int kNV = 2;         // V stages
+constexpr int kNP = 2;         // P buffers
+constexpr uint32_t kTmemCols = 256;
+constexpr int kWarpTma = 4, kWarpMma = 5, kWarpExp = 6;
+
+enum Mode : int { kQuant = 0, kDense = 1 };
+
+// error codes: 0x100 | role << 4 | site
+enum : unsigned { kErrSoftmax = 0x110, kErrTma = 0x120, kErrMma = 0x130, kErrExp = 0x140 };
+
+struct TcParams {
+  AttnParams a;
+  CUtensorMap tm_k0;  // QUANT: MSB plane (u8 [Z,Hkv,N,D/2]); DENSE: K ([Z,Hkv,N,D])
+  CUtensorMap tm_k1;  // QUANT: LSB plane
+  CUtensorMap tm_v;   // V ([Z,Hkv,N,D])
+};
+
+template <int MODE, typename T, int D>
+struct Layout {
+  static constexpr int kAtoms = D / 64;                 // 128-byte K atoms of Q'/K' rows (2D bytes)
+  static constexpr int kQBytes = kAtoms * BM * 128;     // Q' operand
+  static constexpr int kKBytes = kAtoms * BN * 128;     // K' operand stage
+  static constexpr int kStgBytes = (MODE == kQuant) ? BN * D : 0;  // msb + lsb packed
+  static constexpr int kVBytes = (D / 64) * BN * 128;   // V stage (MN-major blocks of 64 dims)
+  static constexpr int kPBytes = BM * 128;              // P stage (64 keys x 2 B per row)
+  static constexpr int oQ = 0;
+  static constexpr int oK = oQ + kQBytes;
+  static constexpr int oV = oK + kNExp * kKBytes;
+  static constexpr int oP = oV + kNV * kVBytes;
+  static constexpr int oStg = oP + kNP * kPBytes;       // 1024-aligned so far
+  static constexpr int oKs = oStg + kNStg * kStgBytes;  // float [kNExp][BN] key scale
+  static constexpr int oKb = oKs + kNExp * BN * 4;      // float [kNExp][BN] key bias * log2e
+  static constexpr int oCs = oKb + kNExp * BN * 4;      // float [2][4][BN] column sums
+  static constexpr int oHs = oCs + 2 * 4 * BN * 4;      // float [4]
+  static constexpr int oBar = oHs + 16;                 // mbarriers
+  static constexpr int kNumBars = 2 * kNStg + 2 * kNExp + 2 * 2 + 2 * kNP + 2 * kNV + 3;
+  static constexpr int oTmem = oBar + kNumBars * 8;
+  static constexpr int oFlag = oTmem + 4;  // int abort, int decision
+  static constexpr int kBytes = oFlag + 16;
+  static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
+};
+
+struct Bars {
+  uint64_t* stg_full;
+  uint64_t* stg_empty;
+  uint64_t* k_full;
+  uint64_t* k_empty;
+  uint64_t* s_full;
+  uint64_t* s_empty;
+  uint64_t* p_full;
+  uint64_t* p_empty;
+  uint64_t* v_full;
+  uint64_t* v_empty;
+  uint64_t* q_ready;
+  uint64_t* dec_ready;
+  uint64_t* o_full;
+};
+
+SPATTEN_DEV uint64_t pack_f2(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+SPATTEN_DEV void unpack_f2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+SPATTEN_DEV uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+SPATTEN_DEV uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// exact int32 -> fp32 for |x| < 2^22 without the conversion pipe:
+// the bits of 1.5 * 2^23 + x, minus 1.5 * 2^23.
+SPATTEN_DEV float i2f_exact(uint32_t x) { return __uint_as_float(x + 0x4B400000u); }
+constexpr float kMagic = 12582912.0f;
+
+template <int MODE, typename T, int D>
+struct Cta {
+  using L = Layout<MODE, T, D>;
+  const TcParams& P;
+  const AttnParams& p;
+  uint8_t* sm;  // 1024-aligned base
+  Bars b;
+  volatile int* abort;
+  int* decision;
+  uint32_t tmem;
+  int z, h, kvh, mt, m0, nt;
+
+  SPATTEN_DEV Cta(const TcParams& pp, uint8_t* base) : P(pp), p(pp.a), sm(base) {
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::oBar);
+    b.stg_full = bar; bar += kNStg;
+    b.stg_empty = bar; bar += kNStg;
+    b.k_full = bar; bar += kNExp;
+    b.k_empty = bar; bar += kNExp;
+    b.s_full = bar; bar += 2;
+    b.s_empty = bar; bar += 2;
+    b.p_full = bar; bar += kNP;
+    b.p_empty = bar; bar += kNP;
+    b.v_full = bar; bar += kNV;
+    b.v_empty = bar; bar += kNV;
+    b.q_ready = bar++;
+    b.dec_ready = bar++;
+    b.o_full = bar++;
+    abort = reinterpret_cast<volatile int*>(sm + L::oFlag);
+    decision = reinterpret_cast<int*>(sm + L::oFlag + 4);
+    mt = blockIdx.x;
+    h = blockIdx.y;
+    z = blockIdx.z;
+    kvh = h / (p.H / p.Hkv);
+    m0 = mt * BM;
+    nt = (p.N + BN - 1) / BN;
+  }
+
+  SPATTEN_DEV void init_barriers() {
+    for (int i = 0; i < kNStg; ++i) {
+      mbar_init(&b.stg_full[i], 1);
+      mbar_init(&b.stg_empty[i], 2);
+    }
+    for (int i = 0; i < kNExp; ++i) {
+      mbar_init(&b.k_full[i], MODE == kQuant ? 2 : 3);
+      mbar_init(&b.k_empty[i], 1 + 4);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&b.s_full[i], 1);
+      mbar_init(&b.s_empty[i], 4);
+    }
+    for (int i = 0; i < kNP; ++i) {
+      mbar_init(&b.p_full[i], 4);
+      mbar_init(&b.p_empty[i], 1);
+    }
+    for (int i = 0; i < kNV; ++i) {
+      mbar_init(&b.v_full[i], 1);
+      mbar_init(&b.v_empty[i], 1);
+    }
+    mbar_init(b.q_ready, 4);
+    mbar_init(b.dec_ready, 4);
+    mbar_init(b.o_full, 1);
+    *abort = 0;
+    *decision = 0;
+    fence_barrier_init();
+  }
+
+  // pass schedule: pass 0 = stats of the MSB score, pass 1 = stats of the
+  // full score (QUANT with a refetched row only), pass 2 = output.
+  SPATTEN_DEV static bool pass_uses_lsb(int pass, int any) {
+    return MODE == kQuant && pass > 0 && any;
+  }
+
+  // ------------------------------------------------------------------ TMA
+  SPATTEN_DEV void tma_role() {
+    if ((threadIdx.x & 31) != 0) return;
+    prefetch_tmap(&P.tm_k0);
+    if (MODE == kQuant) prefetch_tmap(&P.tm_k1);
+    prefetch_tmap(&P.tm_v);
+    uint32_t t = 0, tv = 0;  // global tile counter, V tile counter
+    int any = 0;
+    for (int pass = 0; pass < 3; ++pass) {
+      if (pass == 1) {
+        if (!mbar_wait(b.dec_ready, 0, kErrTma | 1, abort)) break;
+        any = *reinterpret_cast<volatile int*>(decision);
+        if (!(MODE == kQuant && any)) continue;
+      }
+      const bool lsb = pass_uses_lsb(pass, any);
+      bool ok = true;
+      for (int j = 0; j < nt && ok; ++j, ++t) {
+        const int n0 = j * BN;
+        if (MODE == kQuant) {
+          const int s = t % kNStg;
+          if (!mbar_wait(&b.stg_empty[s], ((t / kNStg) & 1) ^ 1, kErrTma | 2, abort)) { ok = false; break; }
+          uint8_t* dst = sm + L::oStg + s * L::kStgBytes;
+          mbar_arrive_expect_tx(&b.stg_full[s], BN * (D / 2) * (lsb ? 2 : 1));
+          tma_load_4d(dst, &P.tm_k0, 0, n0, kvh, z, &b.stg_full[s]);
+          if (lsb) tma_load_4d(dst + BN * (D / 2), &P.tm_k1, 0, n0, kvh, z, &b.stg_full[s]);
+        } else {
+          const int s = t % kNExp;
+          if (!mbar_wait(&b.k_empty[s], ((t / kNExp) & 1) ^ 1, kErrTma | 3, abort)) { ok = false; break; }
+          uint8_t* dst = sm + L::oK + s * L::kKBytes;
+          mbar_arrive_expect_tx(&b.k_full[s], BN * D * 2);
+#pragma unroll
+          for (int a = 0; a < D / 64; ++a)
+            tma_load_4d(dst + a * BN * 128, &P.tm_k0, 64 * a, n0, kvh, z, &b.k_full[s]);
+        }
+        if (pass == 2) {
+          const int s = tv % kNV;
+          if (!mbar_wait(&b.v_empty[s], ((tv / kNV) & 1) ^ 1, kErrTma | 4, abort)) { ok = false; break; }
+          uint8_t* dst = sm + L::oV + s * L::kVBytes;
+          mbar_arrive_expect_tx(&b.v_full[s], BN * D * 2);
+#pragma unroll
+          for (int a = 0; a < D / 64; ++a)
+            tma_load_4d(dst + a * BN * 128, &P.tm_v, 64 * a, n0, kvh, z, &b.v_full[s]);
+          ++tv;
+        }
+      }
+      if (!ok) break;
+    }
+    if (*abort) drain_tma(t, tv);
+  }
+
+  // After an abort: let the copies this thread issued land before the CTA exits.
+  SPATTEN_DEV void drain_tma(uint32_t t, uint32_t tv) {
+    const long long t0 = clock64();
+    auto spin = [&](uint64_t* bar, uint32_t par) {
+      while (!mbar_try_wait(bar, par) && clock64() - t0 < 200000000LL) {
+      }
+    };
+    constexpr uint32_t ring = (MODE == kQuant) ? kNStg : kNExp;
+    for (uint32_t u = (t > ring ? t - ring : 0); u < t; ++u) {
+      if (MODE == kQuant) spin(&b.stg_full[u % kNStg], (u / kNStg) & 1);
+      else spin(&b.k_full[u % kNExp], (u / kNExp) & 1);
+    }
+    for (uint32_t u = (tv > (uint32_t)kNV ? tv - kNV : 0); u < tv; ++u)
+      spin(&b.v_full[u % kNV], (u / kNV) & 1);
+  }
+
+  // ------------------------------------------------------------- expander
+  SPATTEN_DEV void expand_role() {
+    const int e = threadIdx.x - kWarpExp * 32;  // key within the tile, 0..63
+    const int lane = threadIdx.x & 31;
+    const float* ksrc = (MODE == kQuant) ? p.k_scale + ((int64_t)z * p.Hkv + kvh) * p.N : nullptr;
+    const bool key_bias = p.bias != nullptr && p.b_sm == 0;
+    const float* bsrc = key_bias ? p.bias + (int64_t)z * p.b_sz + (int64_t)h * p.b_sh : nullptr;
+    uint32_t t = 0;
+    int any = 0;
+    for (int pass = 0; pass < 3; ++pass) {
+      if (pass == 1) {
+        if (!mbar_wait(b.dec_ready, 0, kErrExp | 1, abort)) return;
+        any = *reinterpret_cast<volatile int*>(decision);
+        if (!(MODE == kQuant && any)) continue;
+      }
+      const bool lsb = pass_uses_lsb(pass, any);
+      for (int j = 0; j < nt; ++j, ++t) {
+        const int n = j * BN + e;
+        const bool valid = n < p.N;
+        float ks = 0.f, kb = 0.f;
+        if (MODE == kQuant && valid) ks = __ldg(ksrc + n);
+        if (key_bias && valid) kb = __ldg(bsrc + (int64_t)n * p.b_sn) * kLog2e;
+        const int es = t % kNExp;
+        uint32_t X[D / 8], Y[D / 8];
+        if (MODE == kQuant) {
+          const int s = t % kNStg;
+          if (!mbar_wait(&b.stg_full[s], (t / kNStg) & 1, kErrExp | 2, abort)) return;
+          const uint4* src = reinterpret_cast<const uint4*>(sm + L::oStg + s * L::kStgBytes + e * (D / 2));
+#pragma unroll
+          for (int i = 0; i < D / 32; ++i) {
+            const uint4 v = src[i];
+            X[4 * i] = v.x; X[4 * i + 1] = v.y; X[4 * i + 2] = v.z; X[4 * i + 3] = v.w;
+          }
+          if (lsb) {
+            const uint4* srcl = reinterpret_cast<const uint4*>(sm + L::oStg + s * L::kStgBytes +
+                                                               BN * (D / 2) + e * (D / 2));
+#pragma unroll
+            for (int i = 0; i < D / 32; ++i) {
+              const uint4 v = srcl[i];
+              Y[4 * i] = v.x; Y[4 * i + 1] = v.y; Y[4 * i + 2] = v.z; Y[4 * i + 3] = v.w;
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&b.stg_empty[s]);
+        }
+        if (!mbar_wait(&b.k_empty[es], ((t / kNExp) & 1) ^ 1, kErrExp | 3, abort)) return;
+        if (MODE == kQuant) {
+          // K' row = [16*msb (D bytes) | lsb (D bytes)], K-major, 128B swizzle
+          uint8_t* row = sm + L::oK + es * L::kKBytes;
+          const int sw = e & 7;
+          auto put = [&](int byte_off, uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+            const int atom = byte_off >> 7, chunk = (byte_off >> 4) & 7;
+            *reinterpret_cast<uint4*>(row + atom * (BN * 128) + e * 128 + ((chunk ^ sw) << 4)) =
+                make_uint4(w0, w1, w2, w3);
+          };
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {  // 16 packed bytes -> 16 dims lo + 16 dims hi
+            const uint32_t* x = X + 4 * c;
+            put(16 * c, (x[0] << 4) & 0xF0F0F0F0u, (x[1] << 4) & 0xF0F0F0F0u,
+                (x[2] << 4) & 0xF0F0F0F0u, (x[3] << 4) & 0xF0F0F0F0u);
+            put(D / 2 + 16 * c, x[0] & 0xF0F0F0F0u, x[1] & 0xF0F0F0F0u, x[2] & 0xF0F0F0F0u,
+                x[3] & 0xF0F0F0F0u);
+            if (lsb) {
+              const uint32_t* y = Y + 4 * c;
+              put(D + 16 * c, y[0] & 0x0F0F0F0Fu, y[1] & 0x0F0F0F0Fu, y[2] & 0x0F0F0F0Fu,
+                  y[3] & 0x0F0F0F0Fu);
+              put(D + D / 2 + 16 * c, (y[0] >> 4) & 0x0F0F0F0Fu, (y[1] >> 4) & 0x0F0F0F0Fu,
+                  (y[2] >> 4) & 0x0F0F0F0Fu, (y[3] >> 4) & 0x0F0F0F0Fu);
+            }
+          }
+          reinterpret_cast<float*>(sm + L::oKs)[es * BN + e] = ks;
+        }
+        reinterpret_cast<float*>(sm + L::oKb)[es * BN + e] = kb;
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&b.k_full[es]);
+      }
+    }
+  }
+
+  // ------------------------------------------------------------------ MMA
+  SPATTEN_DEV void mma_role() {
+    if ((threadIdx.x & 31) != 0) return;
+    constexpr uint32_t ab16 = std::is_same<T, __half>::value ? 0 : 1;
+    constexpr uint32_t idesc_s = (MODE == kQuant) ? instr_desc(2, 1, 0, 0, BM, BN)
+                                                  : instr_desc(1, ab16, 0, 0, BM, BN);
+    constexpr uint32_t idesc_pv = instr_desc(1, ab16, 0, 1, BM, D);
+    const uint32_t qaddr = smem_u32(sm + L::oQ);
+    if (!mbar_wait(b.q_ready, 0, kErrMma | 1, abort)) return;
+    tc_fence_after();
+    uint32_t t = 0, tp = 0, tv = 0;
+    int any = 0;
+    bool first_pv = true;
+    for (int pass = 0; pass < 3; ++pass) {
+      if (pass == 1) {
+        if (!mbar_wait(b.dec_ready, 0, kErrMma | 2, abort)) break;
+        tc_fence_after();
+        any = *reinterpret_cast<volatile int*>(decision);
+        if (!(MODE == kQuant && any)) continue;
+      }
+      // K steps of 32 bytes: QUANT uses D bytes (q8.16msb) or 2D bytes (Q'.K');
+      // DENSE uses 2D bytes (D fp16/bf16 values).
+      const int kbytes = (MODE == kQuant) ? (pass_uses_lsb(pass, any) ? 2 * D : D) : 2 * D;
+      const int nk = kbytes / 32;
+      bool ok = true;
+      for (int j = 0; j <= nt; ++j) {
+        if (j < nt) {
+          const int es = t % kNExp, sb = t & 1;
+          if (!mbar_wait(&b.k_full[es], (t / kNExp) & 1, kErrMma | 3, abort)) { ok = false; break; }
+          if (!mbar_wait(&b.s_empty[sb], ((t >> 1) & 1) ^ 1, kErrMma | 4, abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t kaddr = smem_u32(sm + L::oK + es * L::kKBytes);
+          for (int kk = 0; kk < nk; ++kk) {
+            const int atom = kk >> 2, off = (kk & 3) * 32;
+            const uint64_t ad = smem_desc_sw128(qaddr + atom * (BM * 128) + off, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(kaddr + atom * (BN * 128) + off, 16, 1024);
+            if (MODE == kQuant) mma_i8(tmem + sb * BN, ad, bd, idesc_s, kk > 0);
+            else mma_f16(tmem + sb * BN, ad, bd, idesc_s, kk > 0);
+          }
+          mma_commit(&b.s_full[sb]);
+          mma_commit(&b.k_empty[es]);
+          ++t;
+        }
+        if (pass == 2 && j >= 1) {  // O += P_{j-1} V_{j-1}
+          const int pb = tp % kNP, vs = tv % kNV;
+          if (!mbar_wait(&b.p_full[pb], (tp / kNP) & 1, kErrMma | 5, abort)) { ok = false; break; }
+          if (!mbar_wait(&b.v_full[vs], (tv / kNV) & 1, kErrMma | 6, abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t paddr = smem_u32(sm + L::oP + pb * L::kPBytes);
+          const uint32_t vaddr = smem_u32(sm + L::oV + vs * L::kVBytes);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t ad = smem_desc_sw128(paddr + kk * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(vaddr + kk * 2048, BN * 128, 1024);
+            mma_f16(tmem + 2 * BN, ad, bd, idesc_pv, (first_pv && kk == 0) ? 0u : 1u);
+          }
+          first_pv = false;
+          mma_commit(&b.p_empty[pb]);
+          mma_commit(&b.v_empty[vs]);
+          ++tp;
+          ++tv;
+        }
+        if (pass != 2 && j == nt - 1) break;
+      }
+      if (!ok) break;
+    }
+    // O is complete (or the CTA aborts): signal the epilogue either way, and
+    // wait until every tcgen05 operation issued here has finished before the
+    // CTA can free its tensor memory.
+    mma_commit(b.o_full);
+    const long long t0 = clock64();
+    while (!mbar_try_wait(b.o_full, 0) && clock64() - t0 < kWaitLimitCycles) {
+    }
+  }
+
+  // -------------------------------------------------------------- softmax
+  SPATTEN_DEV void softmax_role();
+  SPATTEN_DEV void load_q_row(int r, bool valid);
+};
+
+// Q row r -> Q' operand (first D bytes for QUANT, 2D bytes for DENSE), zeros if invalid.
+template <int MODE, typename T, int D>
+SPATTEN_DEV void Cta<MODE, T, D>::load_q_row(int r, bool valid) {
+  const int row = m0 + r;
+  uint8_t* base = sm + L::oQ;
+  const int sw = r & 7;
+  const int esz = (MODE == kQuant) ? 1 : (int)sizeof(T);
+  const int bytes = D * esz;  // q row bytes
+  const uint8_t* src = static_cast<const uint8_t*>(p.q) +
+                       ((int64_t)z * p.q_sz + (int64_t)h * p.q_sh + (int64_t)row * p.q_sm) * esz;
+  const bool al16 = ((reinterpret_cast<uintptr_t>(src)) & 15) == 0;
+  for (int c = 0; c < bytes / 16; ++c) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (valid) {
+      if (al16) {
+        v = __ldg(reinterpret_cast<const uint4*>(src) + c);
+      } else {
+        const uint32_t* s4 = reinterpret_cast<const uint32_t*>(src + 16 * c);
+        v = make_uint4(__ldg(s4), __ldg(s4 + 1), __ldg(s4 + 2), __ldg(s4 + 3));
+      }
+    }
+    const int off = 16 * c;
+    const int atom = off >> 7, chunk = (off >> 4) & 7;
+    *reinterpret_cast<uint4*>(base + atom * (BM * 128) + r * 128 + ((chunk ^ sw) << 4)) = v;
+  }
+}
+
+template <int MODE, typename T, int D>
+SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
+  const int r = threadIdx.x;  // row within the tile = TMEM lane
+  const int warp = r >> 5, lane = r & 31;
+  const int row = m0 + r;
+  const bool valid = row < p.M;
+  const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's lane quarter
+  float c2 = 0.f;
+  if (valid) {
+    c2 = (MODE == kQuant) ? p.q_scale[((int64_t)z * p.H + h) * p.M + row] * p.sm_scale * kLog2e
+                          : p.sm_scale * kLog2e;
+  }
+  load_q_row(r, valid);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(b.q_ready);
+
+  const bool key_bias = p.bias != nullptr && p.b_sm == 0;
+  const bool gen_bias = p.bias != nullptr && p.b_sm != 0;
+  const float* brow = gen_bias ? p.bias + (int64_t)z * p.b_sz + (int64_t)h * p.b_sh + (int64_t)row * p.b_sm
+                               : nullptr;
+  const int shift = p.N - p.M;
+  const float* ksm = reinterpret_cast<const float*>(sm + L::oKs);
+  const float* kbm = reinterpret_cast<const float*>(sm + L::oKb);
+
+  uint32_t t = 0;
+  bool alive = true;
+
+  // Tile t's scores (64 columns) from TMEM, as log2-domain floats with the
+  // key scale, the bias and the masks applied. With `dump`, the integer
+  // scores also go to score_out. On an abort the tile is skipped (alive=false).
+  auto scores = [&](int j, float (&s)[BN], int32_t* dump) {
+    const int sb = t & 1, es = t % kNExp;
+    const uint32_t tt = t++;
+    if (!alive) return;
+    if (!mbar_wait(&b.s_full[sb], (tt >> 1) & 1, kErrSoftmax | 1, abort)) { alive = false; return; }
+    tc_fence_after();
+    uint32_t* u = reinterpret_cast<uint32_t*>(s);
+    {
+      uint32_t r0[32], r1[32];
+      tmem_ld32(tl + sb * BN, r0);
+      tmem_ld32(tl + sb * BN + 32, r1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        u[i] = r0[i];
+        u[32 + i] = r1[i];
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&b.s_empty[sb]);
+    const int n0 = j * BN;
+    if (dump && valid) {
+      for (int i = 0; i < BN; ++i)
+        if (n0 + i < p.N) dump[(int64_t)row * p.N + n0 + i] = (int32_t)u[i];
+    }
+    if (!mbar_wait(&b.k_full[es], (tt / kNExp) & 1, kErrSoftmax | 2, abort)) { alive = false; return; }
+    const float* ks = ksm + es * BN;
+    const float* kb = kbm + es * BN;
+    if (MODE == kQuant) {
+      const uint64_t c22 = pack_f2(c2, c2);
+#pragma unroll
+      for (int i = 0; i < BN; i += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(ks + i);
+        const float x0 = i2f_exact(u[i]) - kMagic, x1 = i2f_exact(u[i + 1]) - kMagic;
+        const float x2 = i2f_exact(u[i + 2]) - kMagic, x3 = i2f_exact(u[i + 3]) - kMagic;
+        const uint64_t a = fmul2(fmul2(pack_f2(x0, x1), pack_f2(k4.x, k4.y)), c22);
+        const uint64_t c = fmul2(fmul2(pack_f2(x2, x3), pack_f2(k4.z, k4.w)), c22);
+        unpack_f2(a, s[i], s[i + 1]);
+        unpack_f2(c, s[i + 2], s[i + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < BN; ++i) s[i] = __uint_as_float(u[i]) * c2;
+    }
+    if (key_bias) {
+#pragma unroll
+      for (int i = 0; i < BN; i += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(kb + i);
+        s[i] += k4.x;
+        s[i + 1] += k4.y;
+        s[i + 2] += k4.z;
+        s[i + 3] += k4.w;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&b.k_empty[es]);
+    if (gen_bias && valid) {
+      for (int i = 0; i < BN; ++i)
+        if (n0 + i < p.N) s[i] += __ldg(brow + (int64_t)(n0 + i) * p.b_sn) * kLog2e;
+    }
+    if (n0 + BN > p.N) {
+#pragma unroll
+      for (int i = 0; i < BN; ++i)
+        if (n0 + i >= p.N) s[i] = -INFINITY;
+    }
+    if (p.causal && n0 + BN - 1 > m0 + shift) {
+#pragma unroll
+      for (int i = 0; i < BN; ++i)
+        if (n0 + i > row + shift) s[i] = -INFINITY;
+    }
+  };
+
+  auto stats = [&](const float (&s)[BN], float& m, float& l) {
+    float tmax = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < BN; ++i) tmax = fmaxf(tmax, s[i]);
+    const float mn = fmaxf(m, tmax);
+    if (mn == -INFINITY) return;
+    const float nm = -mn;
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < BN; i += 2) {
+      a0 += fast_exp2(s[i] + nm);
+      a1 += fast_exp2(s[i + 1] + nm);
+    }
+    l = l * fast_exp2(m + nm) + (a0 + a1);
+    m = mn;
+  };
+
+  float s[BN];
+  float m_run = -INFINITY, l_run = 0.f;  // statistics of the scores in use
+  // ---- pass 1: statistics of the MSB (QUANT) / only (DENSE) score
+  for (int j = 0; j < nt; ++j) {
+    scores(j, s, nullptr);
+    if (alive) stats(s, m_run, l_run);
+  }
+  // ---- decide the refetch, build Q'
+  bool flag = false;
+  int any = 0;
+  if (MODE == kQuant) {
+    flag = alive && valid && __frcp_rn(l_run) < p.refetch_thr;
+    // Q' bytes [D, 2D): q8 for a refetched row, zeros otherwise
+    uint8_t* base = sm + L::oQ;
+    const int sw = r & 7;
+#pragma unroll
+    for (int c = 0; c < D / 16; ++c) {
+      const int src_off = 16 * c, dst_off = D + 16 * c;
+      const uint4 v = *reinterpret_cast<const uint4*>(base + (src_off >> 7) * (BM * 128) + r * 128 +
+                                                      ((((src_off >> 4) & 7) ^ sw) << 4));
+      *reinterpret_cast<uint4*>(base + (dst_off >> 7) * (BM * 128) + r * 128 +
+                                ((((dst_off >> 4) & 7) ^ sw) << 4)) =
+          flag ? v : make_uint4(0, 0, 0, 0);
+    }
+    fence_proxy_async_smem();
+    uint32_t anyv;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n barrier.cta.red.or.pred p, 1, 128, q;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(anyv)
+        : "r"((uint32_t)flag)
+        : "memory");
+    any = (int)anyv;
+    if (r == 0) *decision = any;
+    if (p.refetch_out && valid) p.refetch_out[((int64_t)z * p.H + h) * p.M + row] = flag;
+  } else {
+    named_sync(1, 128);
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(b.dec_ready);
+
+  // ---- pass 1b: statistics of the full score for refetched rows
+  if (MODE == kQuant && any) {
+    const bool warp_any = __any_sync(0xffffffffu, flag);
+    float mf = -INFINITY, lf = 0.f;
+    for (int j = 0; j < nt; ++j) {
+      scores(j, s, nullptr);
+      if (alive && warp_any) stats(s, mf, lf);
+    }
+    if (flag) {
+      m_run = mf;
+      l_run = lf;
+    }
+  }
+
+  // ---- pass 2: P, V prune, importance, P.V
+  const float inv_l = (valid && m_run != -INFINITY && l_run > 0.f) ? 1.f / l_run : 0.f;
+  const float mneg = (m_run == -INFINITY) ? 0.f : -m_run;
+  const bool want_tok = p.tok_partial != nullptr;
+  float* tokp = want_tok ? p.tok_partial + (((int64_t)z * p.H + h) * p.mtiles + mt) * p.N : nullptr;
+  float* cs = reinterpret_cast<float*>(sm + L::oCs);
+  const float vthr = p.v_thr;
+  int32_t* dump = (MODE == kQuant && p.score_out)
+                      ? p.score_out + ((int64_t)z * p.H + h) * p.M * (int64_t)p.N
+                      : nullptr;
+  const uint64_t inv2 = pack_f2(inv_l, inv_l);
+  const uint64_t mn2 = pack_f2(mneg, mneg);
+  for (int j = 0; j < nt; ++j) {
+    const int pb = j % kNP;
+    scores(j, s, dump);
+    if (alive) {
+#pragma unroll
+      for (int i = 0; i < BN; i += 2) {
+        float a0, a1;
+        unpack_f2(fadd2(pack_f2(s[i], s[i + 1]), mn2), a0, a1);
+        unpack_f2(fmul2(pack_f2(fast_exp2(a0), fast_exp2(a1)), inv2), s[i], s[i + 1]);
+      }
+      if (vthr > 0.f) {
+#pragma unroll
+        for (int i = 0; i < BN; ++i) s[i] = s[i] < vthr ? 0.f : s[i];
+      }
+      // P -> shared memory (A operand of P.V, K-major, 128B swizzle)
+      if (mbar_wait(&b.p_empty[pb], ((j / kNP) & 1) ^ 1, kErrSoftmax | 3, abort)) {
+        uint8_t* prow = sm + L::oP + pb * L::kPBytes + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 v;
+          v.x = pack2<T>(s[8 * c], s[8 * c + 1]);
+          v.y = pack2<T>(s[8 * c + 2], s[8 * c + 3]);
+          v.z = pack2<T>(s[8 * c + 4], s[8 * c + 5]);
+          v.w = pack2<T>(s[8 * c + 6], s[8 * c + 7]);
+          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&b.p_full[pb]);
+      } else {
+        alive = false;
+      }
+    }
+    if (want_tok) {
+      // column sums of this warp's 32 rows (P is in shared memory already, so
+      // s is reduced in place): reduce-scatter over the lanes, lane l ends
+      // with column (half*32 + l)
+      float* csb = cs + (j & 1) * 4 * BN + warp * BN;
+      if (!alive) {
+#pragma unroll
+        for (int i = 0; i < BN; ++i) s[i] = 0.f;
+      }
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float* v = s + half * 32;
+#pragma unroll
+        for (int w = 16; w >= 1; w >>= 1) {
+          const bool up = lane & w;
+#pragma unroll
+          for (int i = 0; i < w; ++i) {
+            const float send = up ? v[i] : v[i + w];
+            const float keep = up ? v[i + w] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+          }
+        }
+        csb[half * 32 + lane] = v[0];
+      }
+      named_sync(1, 128);
+      if (r < BN && alive) {
+        const float* c0 = cs + (j & 1) * 4 * BN;
+        const int key = j * BN + r;
+        if (key < p.N) tokp[key] = ((c0[r] + c0[BN + r]) + c0[2 * BN + r]) + c0[3 * BN + r];
+      }
+    }
+  }
+
+  // ---- epilogue: O (already normalised) from TMEM
+  if (!mbar_wait(b.o_full, 0, kErrSoftmax | 4, abort)) alive = false;
+  tc_fence_after();
+  float asum = 0.f;
+  const int hslot = p.out_head_map ? p.out_head_map[h] : h;
+  const bool out_ok = hslot >= 0 && hslot < p.out_head_slots;
+  T* orow = static_cast<T*>(p.out) + (int64_t)z * p.o_sz + (int64_t)hslot * p.o_sh + (int64_t)row * p.o_sm;
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t o[32];
+    tmem_ld32(tl + 2 * BN + 32 * c, o);
+    tmem_wait_ld();
+    if (alive && valid) {
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float x0 = __uint_as_float(o[2 * i]), x1 = __uint_as_float(o[2 * i + 1]);
+        asum += fabsf(x0) + fabsf(x1);
+        pk[i] = pack2<T>(x0, x1);
+      }
+      if (out_ok) {
+        uint32_t* dst = reinterpret_cast<uint32_t*>(orow + 32 * c);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) dst[i] = pk[i];
+      }
+    }
+  }
+  tc_fence_before();
+  if (p.head_partial) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) asum += __shfl_xor_sync(0xffffffffu, asum, off);
+    float* hs = reinterpret_cast<float*>(sm + L::oHs);
+    if (lane == 0) hs[warp] = asum;
+    named_sync(1, 128);
+    if (r == 0 && alive)
+      p.head_partial[((int64_t)z * p.H + h) * p.mtiles + mt] = ((hs[0] + hs[1]) + hs[2]) + hs[3];
+  }
+}
+
+template <int MODE, typename T, int D>
+__global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
+    prog_attn_tc_kernel(const __grid_constant__ TcParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  using L = Layout<MODE, T, D>;
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  Cta<MODE, T, D> c(P, base);
+  const int warp = threadIdx.x >> 5;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(base + L::oTmem);
+  if (threadIdx.x == 0) c.init_barriers();
+  if (warp == kWarpMma) {
+    tmem_alloc(tslot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  c.tmem = *tslot;
+  if (warp < 4) c.softmax_role();
+  else if (warp == kWarpTma) c.tma_role();
+  else if (warp == kWarpMma) c.mma_role();
+  else c.expand_role();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(c.tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 4-D map [Z, H, N, inner] with byte strides (sn, sh, sz); box {box_inner, 64, 1, 1}.
+cudaError_t make_map(CUtensorMap* m, CUtensorMapDataType dt, int esz, const void* base, int inner,
+                     int N, int H, int Z, int64_t sn, int64_t sh, int64_t sz, int box_inner,
+                     CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  auto fix = [](int64_t s, int64_t minv) -> cuuint64_t { return (cuuint64_t)(s > 0 ? s : minv); };
+  cuuint64_t dims[4] = {(cuuint64_t)inner, (cuuint64_t)N, (cuuint64_t)H, (cuuint64_t)Z};
+  cuuint64_t strides[3] = {fix(sn, 16), fix(sh, 16), fix(sz, 16)};
+  cuuint32_t box[4] = {(cuuint32_t)box_inner, (cuuint32_t)BN, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  (void)esz;
+  CUresult r = fn(m, dt, 4, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int MODE, typename T, int D>
+cudaError_t launch_tc_t(const AttnParams& a, cudaStream_t st) {
+  using L = Layout<MODE, T, D>;
+  TcParams P;
+  memset(&P, 0, sizeof(P));
+  P.a = a;
+  const CUtensorMapDataType vdt =
+      std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cudaError_t e;
+  if (MODE == kQuant) {
+    e = make_map(&P.tm_k0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.k0, D / 2, a.N, a.Hkv, a.Z, a.k_sn,
+                 a.k_sh, a.k_sz, D / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (e != cudaSuccess) return e;
+    e = make_map(&P.tm_k1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.k1, D / 2, a.N, a.Hkv, a.Z, a.k_sn,
+                 a.k_sh, a.k_sz, D / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (e != cudaSuccess) return e;
+  } else {
+    e = make_map(&P.tm_k0, vdt, 2, a.k0, D, a.N, a.Hkv, a.Z, a.k_sn * 2, a.k_sh * 2, a.k_sz * 2, 64,
+                 CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e != cudaSuccess) return e;
+  }
+  e = make_map(&P.tm_v, vdt, 2, a.v, D, a.N, a.Hkv, a.Z, a.v_sn * 2, a.v_sh * 2, a.v_sz * 2, 64,
+               CU_TENSOR_MAP_SWIZZLE_128B);
+  if (e != cudaSuccess) return e;
+  auto kern = prog_attn_tc_kernel<MODE, T, D>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)a.mtiles, (unsigned)a.H, (unsigned)a.Z);
+  kern<<<grid, kThreads, L::kAlloc, st>>>(P);
+  return cudaGetLastError();
+}
+
+template <int MODE, typename T>
+cudaError_t launch_tc_d(const AttnParams& a, cudaStream_t st) {
+  if (a.D == 64) return launch_tc_t<MODE, T, 64>(a, st);
+  if (a.D == 128) return launch_tc_t<MODE, T, 128>(a, st);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int tc_tile_rows() { return BM; }
+
+cudaError_t launch_prog_attn_tc(const AttnParams& a, cudaStream_t st) {
+  const bool f16 = a.dtype == kF16;
+  if (a.mode == kQuant) return f16 ? launch_tc_d<kQuant, __half>(a, st) : launch_tc_d<kQuant, __nv_bfloat16>(a, st);
+  if (a.mode == kDense) return f16 ? launch_tc_d<kDense, __half>(a, st) : launch_tc_d<kDense, __nv_bfloat16>(a, st);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t read_device_error(unsigned int* code, bool reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(code, sm100::g_device_error, sizeof(unsigned int));
+  if (e != cudaSuccess || !reset) return e;
+  const unsigned int zero = 0;
+  return cudaMemcpyToSymbol(sm100::g_device_error, &zero, sizeof(unsigned int));
+}
+
+}  // namespace spatten

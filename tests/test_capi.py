@@ -67,7 +67,7 @@ def test_workspace_size_matches_partials():
     a.tok_out = 1 << 21
     a.head_out = 1 << 22
     ws = N.lib.spatten_prog_attn_workspace_size(a)
-    mtiles = (100 + 63) // 64
+    mtiles = (100 + 127) // 128  # QUANT/DENSE: 128 query rows per CTA
     tok = 2 * 4 * mtiles * 257 * 4
     head = 2 * 4 * mtiles * 4
     r = lambda x: (x + 255) // 256 * 256  # noqa: E731
