@@ -102,21 +102,23 @@ struct Bars {
   uint64_t* o_full;
 };
 
-SPATTEN_DEV uint64_t pack_f2(float lo, float hi) {
-  uint64_t d;
+// Pairs of fp32 values for the packed (f32x2) FP instructions of sm_100.
+using f2 = uint64_t;
+SPATTEN_DEV f2 pack_f2(float lo, float hi) {
+  f2 d;
   asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
   return d;
 }
-SPATTEN_DEV void unpack_f2(uint64_t v, float& lo, float& hi) {
+SPATTEN_DEV void unpack_f2(f2 v, float& lo, float& hi) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
 }
-SPATTEN_DEV uint64_t fmul2(uint64_t a, uint64_t b) {
-  uint64_t d;
+SPATTEN_DEV f2 fmul2(f2 a, f2 b) {
+  f2 d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-SPATTEN_DEV uint64_t fadd2(uint64_t a, uint64_t b) {
-  uint64_t d;
+SPATTEN_DEV f2 fadd2(f2 a, f2 b) {
+  f2 d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
@@ -280,21 +282,33 @@ struct Cta {
         if (!(MODE == kQuant && any)) continue;
       }
       const bool lsb = pass_uses_lsb(pass, any);
-      for (int j = 0; j < nt; ++j, ++t) {
+      // key scale / bias of tile j, loaded one tile ahead to hide the latency
+      auto fetch = [&](int j, float& ks, float& kb) {
         const int n = j * BN + e;
-        const bool valid = n < p.N;
-        float ks = 0.f, kb = 0.f;
-        if (MODE == kQuant && valid) ks = __ldg(ksrc + n);
-        if (key_bias && valid) kb = __ldg(bsrc + (int64_t)n * p.b_sn) * kLog2e;
+        ks = 0.f;
+        kb = 0.f;
+        if (j < nt && n < p.N) {
+          if (MODE == kQuant) ks = __ldg(ksrc + n);
+          if (key_bias) kb = __ldg(bsrc + (int64_t)n * p.b_sn) * kLog2e;
+        }
+      };
+      float ks_next, kb_next;
+      fetch(0, ks_next, kb_next);
+      for (int j = 0; j < nt; ++j, ++t) {
+        const float ks = ks_next, kb = kb_next;
+        fetch(j + 1, ks_next, kb_next);
         const int es = t % kNExp;
         uint32_t X[D / 8], Y[D / 8];
         if (MODE == kQuant) {
           const int s = t % kNStg;
           if (!mbar_wait(&b.stg_full[s], (t / kNStg) & 1, kErrExp | 2, abort)) return;
+          // staging rows of D/2 bytes land with the TMA's 32-byte (D=64) or
+          // 64-byte (D=128) swizzle: 16-byte chunk c of row e sits at c ^ sw
+          const int sw = (D == 64) ? ((e >> 2) & 1) : ((e >> 1) & 3);
           const uint4* src = reinterpret_cast<const uint4*>(sm + L::oStg + s * L::kStgBytes + e * (D / 2));
 #pragma unroll
           for (int i = 0; i < D / 32; ++i) {
-            const uint4 v = src[i];
+            const uint4 v = src[i ^ sw];
             X[4 * i] = v.x; X[4 * i + 1] = v.y; X[4 * i + 2] = v.z; X[4 * i + 3] = v.w;
           }
           if (lsb) {
@@ -302,7 +316,7 @@ struct Cta {
                                                                BN * (D / 2) + e * (D / 2));
 #pragma unroll
             for (int i = 0; i < D / 32; ++i) {
-              const uint4 v = srcl[i];
+              const uint4 v = srcl[i ^ sw];
               Y[4 * i] = v.x; Y[4 * i + 1] = v.y; Y[4 * i + 2] = v.z; Y[4 * i + 3] = v.w;
             }
           }
@@ -512,14 +526,14 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
     const float* ks = ksm + es * BN;
     const float* kb = kbm + es * BN;
     if (MODE == kQuant) {
-      const uint64_t c22 = pack_f2(c2, c2);
+      const f2 c22 = pack_f2(c2, c2);
 #pragma unroll
       for (int i = 0; i < BN; i += 4) {
         const float4 k4 = *reinterpret_cast<const float4*>(ks + i);
         const float x0 = i2f_exact(u[i]) - kMagic, x1 = i2f_exact(u[i + 1]) - kMagic;
         const float x2 = i2f_exact(u[i + 2]) - kMagic, x3 = i2f_exact(u[i + 3]) - kMagic;
-        const uint64_t a = fmul2(fmul2(pack_f2(x0, x1), pack_f2(k4.x, k4.y)), c22);
-        const uint64_t c = fmul2(fmul2(pack_f2(x2, x3), pack_f2(k4.z, k4.w)), c22);
+        const f2 a = fmul2(fmul2(pack_f2(x0, x1), pack_f2(k4.x, k4.y)), c22);
+        const f2 c = fmul2(fmul2(pack_f2(x2, x3), pack_f2(k4.z, k4.w)), c22);
         unpack_f2(a, s[i], s[i + 1]);
         unpack_f2(c, s[i + 2], s[i + 3]);
       }
@@ -543,93 +557,62 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
       for (int i = 0; i < BN; ++i)
         if (n0 + i < p.N) s[i] += __ldg(brow + (int64_t)(n0 + i) * p.b_sn) * kLog2e;
     }
-    if (n0 + BN > p.N) {
+    // keys past N and, with the causal mask, keys after the row's diagonal:
+    // only tiles that reach them pay for the per-element test
+    int lim = p.N - n0;
+    if (p.causal) lim = min(lim, row + shift + 1 - n0);
+    if (lim < BN) {
 #pragma unroll
       for (int i = 0; i < BN; ++i)
-        if (n0 + i >= p.N) s[i] = -INFINITY;
-    }
-    if (p.causal && n0 + BN - 1 > m0 + shift) {
-#pragma unroll
-      for (int i = 0; i < BN; ++i)
-        if (n0 + i > row + shift) s[i] = -INFINITY;
+        if (i >= lim) s[i] = -INFINITY;
     }
   };
 
+  // Online row statistics over one tile. Eight independent max / sum chains
+  // keep the dependent-latency per tile short.
   auto stats = [&](const float (&s)[BN], float& m, float& l) {
-    float tmax = -INFINITY;
+    float mx[8];
 #pragma unroll
-    for (int i = 0; i < BN; ++i) tmax = fmaxf(tmax, s[i]);
+    for (int k = 0; k < 8; ++k) mx[k] = s[k];
+#pragma unroll
+    for (int i = 8; i < BN; i += 8)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], s[i + k]);
+    const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
     const float mn = fmaxf(m, tmax);
     if (mn == -INFINITY) return;
-    const float nm = -mn;
-    float a0 = 0.f, a1 = 0.f;
+    const f2 nm2 = pack_f2(-mn, -mn);
+    f2 acc[4];
 #pragma unroll
-    for (int i = 0; i < BN; i += 2) {
-      a0 += fast_exp2(s[i] + nm);
-      a1 += fast_exp2(s[i + 1] + nm);
+    for (int k = 0; k < 4; ++k) {
+      float a0, a1;
+      unpack_f2(fadd2(pack_f2(s[2 * k], s[2 * k + 1]), nm2), a0, a1);
+      acc[k] = pack_f2(fast_exp2(a0), fast_exp2(a1));
     }
-    l = l * fast_exp2(m + nm) + (a0 + a1);
+#pragma unroll
+    for (int i = 8; i < BN; i += 8)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float a0, a1;
+        unpack_f2(fadd2(pack_f2(s[i + 2 * k], s[i + 2 * k + 1]), nm2), a0, a1);
+        acc[k] = fadd2(acc[k], pack_f2(fast_exp2(a0), fast_exp2(a1)));
+      }
+    float t0, t1, t2, t3, t4, t5, t6, t7;
+    unpack_f2(acc[0], t0, t1);
+    unpack_f2(acc[1], t2, t3);
+    unpack_f2(acc[2], t4, t5);
+    unpack_f2(acc[3], t6, t7);
+    const float sum = ((t0 + t1) + (t2 + t3)) + ((t4 + t5) + (t6 + t7));
+    l = l * fast_exp2(m - mn) + sum;
     m = mn;
   };
 
   float s[BN];
   float m_run = -INFINITY, l_run = 0.f;  // statistics of the scores in use
-  // ---- pass 1: statistics of the MSB (QUANT) / only (DENSE) score
-  for (int j = 0; j < nt; ++j) {
-    scores(j, s, nullptr);
-    if (alive) stats(s, m_run, l_run);
-  }
-  // ---- decide the refetch, build Q'
-  bool flag = false;
+  float mf = -INFINITY, lf = 0.f;        // statistics of the full score (pass 1b)
+  bool flag = false, warp_any = false;
   int any = 0;
-  if (MODE == kQuant) {
-    flag = alive && valid && __frcp_rn(l_run) < p.refetch_thr;
-    // Q' bytes [D, 2D): q8 for a refetched row, zeros otherwise
-    uint8_t* base = sm + L::oQ;
-    const int sw = r & 7;
-#pragma unroll
-    for (int c = 0; c < D / 16; ++c) {
-      const int src_off = 16 * c, dst_off = D + 16 * c;
-      const uint4 v = *reinterpret_cast<const uint4*>(base + (src_off >> 7) * (BM * 128) + r * 128 +
-                                                      ((((src_off >> 4) & 7) ^ sw) << 4));
-      *reinterpret_cast<uint4*>(base + (dst_off >> 7) * (BM * 128) + r * 128 +
-                                ((((dst_off >> 4) & 7) ^ sw) << 4)) =
-          flag ? v : make_uint4(0, 0, 0, 0);
-    }
-    fence_proxy_async_smem();
-    uint32_t anyv;
-    asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n barrier.cta.red.or.pred p, 1, 128, q;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(anyv)
-        : "r"((uint32_t)flag)
-        : "memory");
-    any = (int)anyv;
-    if (r == 0) *decision = any;
-    if (p.refetch_out && valid) p.refetch_out[((int64_t)z * p.H + h) * p.M + row] = flag;
-  } else {
-    named_sync(1, 128);
-  }
-  __syncwarp();
-  if (lane == 0) mbar_arrive(b.dec_ready);
-
-  // ---- pass 1b: statistics of the full score for refetched rows
-  if (MODE == kQuant && any) {
-    const bool warp_any = __any_sync(0xffffffffu, flag);
-    float mf = -INFINITY, lf = 0.f;
-    for (int j = 0; j < nt; ++j) {
-      scores(j, s, nullptr);
-      if (alive && warp_any) stats(s, mf, lf);
-    }
-    if (flag) {
-      m_run = mf;
-      l_run = lf;
-    }
-  }
-
-  // ---- pass 2: P, V prune, importance, P.V
-  const float inv_l = (valid && m_run != -INFINITY && l_run > 0.f) ? 1.f / l_run : 0.f;
-  const float mneg = (m_run == -INFINITY) ? 0.f : -m_run;
   const bool want_tok = p.tok_partial != nullptr;
   float* tokp = want_tok ? p.tok_partial + (((int64_t)z * p.H + h) * p.mtiles + mt) * p.N : nullptr;
   float* cs = reinterpret_cast<float*>(sm + L::oCs);
@@ -637,70 +620,136 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
   int32_t* dump = (MODE == kQuant && p.score_out)
                       ? p.score_out + ((int64_t)z * p.H + h) * p.M * (int64_t)p.N
                       : nullptr;
-  const uint64_t inv2 = pack_f2(inv_l, inv_l);
-  const uint64_t mn2 = pack_f2(mneg, mneg);
-  for (int j = 0; j < nt; ++j) {
-    const int pb = j % kNP;
-    scores(j, s, dump);
-    if (alive) {
+  f2 inv2 = pack_f2(0.f, 0.f), mn2 = pack_f2(0.f, 0.f);
+  // One loop over the passes keeps a single copy of the tile code:
+  //   pass 0 statistics of the MSB (QUANT) / only (DENSE) score
+  //   pass 1 statistics of the full score of refetched rows (QUANT, if any)
+  //   pass 2 P, V prune, P -> shared memory, column sums
+  for (int pass = 0; pass < 3; ++pass) {
+    if (pass == 1) {
+      // ---- decide the refetch, build Q'
+      if (MODE == kQuant) {
+        flag = alive && valid && __frcp_rn(l_run) < p.refetch_thr;
+        // Q' bytes [D, 2D): q8 for a refetched row, zeros otherwise
+        uint8_t* base = sm + L::oQ;
+        const int sw = r & 7;
 #pragma unroll
-      for (int i = 0; i < BN; i += 2) {
-        float a0, a1;
-        unpack_f2(fadd2(pack_f2(s[i], s[i + 1]), mn2), a0, a1);
-        unpack_f2(fmul2(pack_f2(fast_exp2(a0), fast_exp2(a1)), inv2), s[i], s[i + 1]);
-      }
-      if (vthr > 0.f) {
-#pragma unroll
-        for (int i = 0; i < BN; ++i) s[i] = s[i] < vthr ? 0.f : s[i];
-      }
-      // P -> shared memory (A operand of P.V, K-major, 128B swizzle)
-      if (mbar_wait(&b.p_empty[pb], ((j / kNP) & 1) ^ 1, kErrSoftmax | 3, abort)) {
-        uint8_t* prow = sm + L::oP + pb * L::kPBytes + r * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 v;
-          v.x = pack2<T>(s[8 * c], s[8 * c + 1]);
-          v.y = pack2<T>(s[8 * c + 2], s[8 * c + 3]);
-          v.z = pack2<T>(s[8 * c + 4], s[8 * c + 5]);
-          v.w = pack2<T>(s[8 * c + 6], s[8 * c + 7]);
-          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = v;
+        for (int c = 0; c < D / 16; ++c) {
+          const int src_off = 16 * c, dst_off = D + 16 * c;
+          const uint4 v = *reinterpret_cast<const uint4*>(base + (src_off >> 7) * (BM * 128) + r * 128 +
+                                                          ((((src_off >> 4) & 7) ^ sw) << 4));
+          *reinterpret_cast<uint4*>(base + (dst_off >> 7) * (BM * 128) + r * 128 +
+                                    ((((dst_off >> 4) & 7) ^ sw) << 4)) =
+              flag ? v : make_uint4(0, 0, 0, 0);
         }
         fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&b.p_full[pb]);
+        uint32_t anyv;
+        asm volatile(
+            "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n barrier.cta.red.or.pred p, 1, 128, q;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(anyv)
+            : "r"((uint32_t)flag)
+            : "memory");
+        any = (int)anyv;
+        if (r == 0) *decision = any;
+        if (p.refetch_out && valid) p.refetch_out[((int64_t)z * p.H + h) * p.M + row] = flag;
       } else {
-        alive = false;
+        named_sync(1, 128);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b.dec_ready);
+      if (!(MODE == kQuant && any)) continue;
+      warp_any = __any_sync(0xffffffffu, flag);
     }
-    if (want_tok) {
-      // column sums of this warp's 32 rows (P is in shared memory already, so
-      // s is reduced in place): reduce-scatter over the lanes, lane l ends
-      // with column (half*32 + l)
-      float* csb = cs + (j & 1) * 4 * BN + warp * BN;
-      if (!alive) {
-#pragma unroll
-        for (int i = 0; i < BN; ++i) s[i] = 0.f;
+    if (pass == 2) {
+      if (MODE == kQuant && any && flag) {
+        m_run = mf;
+        l_run = lf;
       }
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float* v = s + half * 32;
-#pragma unroll
-        for (int w = 16; w >= 1; w >>= 1) {
-          const bool up = lane & w;
-#pragma unroll
-          for (int i = 0; i < w; ++i) {
-            const float send = up ? v[i] : v[i + w];
-            const float keep = up ? v[i + w] : v[i];
-            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+      const float inv_l = (valid && m_run != -INFINITY && l_run > 0.f) ? 1.f / l_run : 0.f;
+      const float mneg = (m_run == -INFINITY) ? 0.f : -m_run;
+      inv2 = pack_f2(inv_l, inv_l);
+      mn2 = pack_f2(mneg, mneg);
+    }
+    for (int j = 0; j < nt; ++j) {
+      scores(j, s, pass == 2 ? dump : nullptr);
+      if (pass < 2) {
+        if (alive && (pass == 0 || warp_any)) {
+          float m = pass == 0 ? m_run : mf;
+          float l = pass == 0 ? l_run : lf;
+          stats(s, m, l);
+          if (pass == 0) {
+            m_run = m;
+            l_run = l;
+          } else {
+            mf = m;
+            lf = l;
           }
         }
-        csb[half * 32 + lane] = v[0];
+        continue;
       }
-      named_sync(1, 128);
-      if (r < BN && alive) {
-        const float* c0 = cs + (j & 1) * 4 * BN;
-        const int key = j * BN + r;
-        if (key < p.N) tokp[key] = ((c0[r] + c0[BN + r]) + c0[2 * BN + r]) + c0[3 * BN + r];
+      // ---- pass 2 tile
+      const int pb = j % kNP;
+      if (alive) {
+#pragma unroll
+        for (int i = 0; i < BN; i += 2) {
+          float a0, a1;
+          unpack_f2(fadd2(pack_f2(s[i], s[i + 1]), mn2), a0, a1);
+          unpack_f2(fmul2(pack_f2(fast_exp2(a0), fast_exp2(a1)), inv2), s[i], s[i + 1]);
+        }
+        if (vthr > 0.f) {
+#pragma unroll
+          for (int i = 0; i < BN; ++i) s[i] = s[i] < vthr ? 0.f : s[i];
+        }
+        // P -> shared memory (A operand of P.V, K-major, 128B swizzle)
+        if (mbar_wait(&b.p_empty[pb], ((j / kNP) & 1) ^ 1, kErrSoftmax | 3, abort)) {
+          uint8_t* prow = sm + L::oP + pb * L::kPBytes + r * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint4 v;
+            v.x = pack2<T>(s[8 * c], s[8 * c + 1]);
+            v.y = pack2<T>(s[8 * c + 2], s[8 * c + 3]);
+            v.z = pack2<T>(s[8 * c + 4], s[8 * c + 5]);
+            v.w = pack2<T>(s[8 * c + 6], s[8 * c + 7]);
+            *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = v;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&b.p_full[pb]);
+        } else {
+          alive = false;
+        }
+      }
+      if (want_tok) {
+        // column sums of this warp's 32 rows (P is in shared memory already, so
+        // s is reduced in place): reduce-scatter over the lanes, lane l ends
+        // with column (half*32 + l)
+        float* csb = cs + (j & 1) * 4 * BN + warp * BN;
+        if (!alive) {
+#pragma unroll
+          for (int i = 0; i < BN; ++i) s[i] = 0.f;
+        }
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float* v = s + half * 32;
+#pragma unroll
+          for (int w = 16; w >= 1; w >>= 1) {
+            const bool up = lane & w;
+#pragma unroll
+            for (int i = 0; i < w; ++i) {
+              const float send = up ? v[i] : v[i + w];
+              const float keep = up ? v[i + w] : v[i];
+              v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+            }
+          }
+          csb[half * 32 + lane] = v[0];
+        }
+        named_sync(1, 128);
+        if (r < BN && alive) {
+          const float* c0 = cs + (j & 1) * 4 * BN;
+          const int key = j * BN + r;
+          if (key < p.N) tokp[key] = ((c0[r] + c0[BN + r]) + c0[2 * BN + r]) + c0[3 * BN + r];
+        }
       }
     }
   }
@@ -712,6 +761,7 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
   const int hslot = p.out_head_map ? p.out_head_map[h] : h;
   const bool out_ok = hslot >= 0 && hslot < p.out_head_slots;
   T* orow = static_cast<T*>(p.out) + (int64_t)z * p.o_sz + (int64_t)hslot * p.o_sh + (int64_t)row * p.o_sm;
+  const bool out16 = (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
 #pragma unroll
   for (int c = 0; c < D / 32; ++c) {
     uint32_t o[32];
@@ -726,9 +776,15 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
         pk[i] = pack2<T>(x0, x1);
       }
       if (out_ok) {
-        uint32_t* dst = reinterpret_cast<uint32_t*>(orow + 32 * c);
+        if (out16) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) dst[i] = pk[i];
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        } else {
+          uint32_t* dst = reinterpret_cast<uint32_t*>(orow + 32 * c);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) dst[i] = pk[i];
+        }
       }
     }
   }
@@ -815,11 +871,12 @@ cudaError_t launch_tc_t(const AttnParams& a, cudaStream_t st) {
       std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   cudaError_t e;
   if (MODE == kQuant) {
+    const CUtensorMapSwizzle psw = (D == 64) ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
     e = make_map(&P.tm_k0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.k0, D / 2, a.N, a.Hkv, a.Z, a.k_sn,
-                 a.k_sh, a.k_sz, D / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+                 a.k_sh, a.k_sz, D / 2, psw);
     if (e != cudaSuccess) return e;
     e = make_map(&P.tm_k1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.k1, D / 2, a.N, a.Hkv, a.Z, a.k_sn,
-                 a.k_sh, a.k_sz, D / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+                 a.k_sh, a.k_sz, D / 2, psw);
     if (e != cudaSuccess) return e;
   } else {
     e = make_map(&P.tm_k0, vdt, 2, a.k0, D, a.N, a.Hkv, a.Z, a.k_sn * 2, a.k_sh * 2, a.k_sz * 2, 64,

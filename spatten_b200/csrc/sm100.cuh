@@ -56,7 +56,11 @@ SPATTEN_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int code,
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    // try_wait suspends the thread for a while by itself; the abort flag and
+    // the clock are checked once per batch of polls.
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
     if (clock64() - t0 > kWaitLimitCycles) {
       record_error(code);
