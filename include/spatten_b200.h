@@ -139,6 +139,23 @@ int spatten_prog_attn(const spatten_prog_attn_args* a, void* workspace, size_t w
                       void* stream);
 
 /*
+ * Allocation-free spatten_prog_attn, for callers that cannot call cudaMalloc:
+ * hosts that fix their device-memory budget at start-up and forbid allocation
+ * afterwards, and plugins limited to the memory their host hands them. No
+ * counterpart in the reference, which has no C interface.
+ *
+ * The workspace comes from a fixed array of
+ * spatten_prog_attn_noalloc_capacity() bytes (16 MiB) in device memory that
+ * the library holds on every GPU that loads it, until the process exits; a
+ * request needing more (spatten_prog_attn_workspace_size) fails with
+ * SPATTEN_ERR_INVALID. Calls on one device share the array: calls that may
+ * overlap on the GPU race, so order them on one stream. The first call on a
+ * device looks up the array's address; make it before any stream capture.
+ */
+size_t spatten_prog_attn_noalloc_capacity(void);
+int spatten_prog_attn_noalloc(const spatten_prog_attn_args* a, void* stream);
+
+/*
  * Top-k selection, indices returned in ascending order:
  *   out[r, :] = sort(topk(x[r, :n], k).indices), r < rows
  * Ties at the k-th value go to the smaller index. x fp32 with row stride

@@ -56,6 +56,8 @@ SIGNATURES = {
                                        c_i64, c_vp, c_vp, c_vp, c_vp]),
     "spatten_prog_attn_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(ProgAttnArgs)]),
     "spatten_prog_attn": (c_int, [ctypes.POINTER(ProgAttnArgs), c_vp, ctypes.c_size_t, c_vp]),
+    "spatten_prog_attn_noalloc_capacity": (ctypes.c_size_t, []),
+    "spatten_prog_attn_noalloc": (c_int, [ctypes.POINTER(ProgAttnArgs), c_vp]),
     "spatten_topk_indices": (c_int, [c_vp, c_int, c_int, c_i64, c_int, c_vp, c_vp]),
     "spatten_gather_rows": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_int, c_int, c_int,
                                     c_i64, c_i64, c_vp, c_i64, c_i64, c_vp]),

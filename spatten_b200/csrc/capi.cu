@@ -69,6 +69,11 @@ int check_quant_args(const void* x, int dtype, int Z, int H, int M, int D, int64
 
 }  // namespace
 
+int spatten::set_last_error(int code, const char* msg) {
+  g_err = msg ? msg : "";
+  return code;
+}
+
 extern "C" {
 
 int spatten_abi_version(void) { return 1; }

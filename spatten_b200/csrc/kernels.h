@@ -51,6 +51,9 @@ cudaError_t launch_prog_attn_mma(const AttnParams& p, cudaStream_t st);
 // device error word written by a kernel whose bounded wait ran out
 cudaError_t read_device_error(unsigned int* code, bool reset);
 
+// Record `msg` as the calling thread's spatten_last_error() and return `code`.
+int set_last_error(int code, const char* msg);
+
 cudaError_t launch_importance_reduce(const float* tok_partial, const float* head_partial, int Z,
                                      int H, int mtiles, int N, const float* tok_in,
                                      float* tok_out, float* head_out, cudaStream_t st);
