@@ -90,7 +90,19 @@ def _attention_core_quant(q, k, v, mask, sm_scale, refetch_thr, v_thr):
     return ctx, tok, r
 
 
-def self_attention(attn, hidden, mask, active_heads, cumulative, kn: LayerKnobs):
+def _topk_sorted(x, k, tie_rule):
+    """sort(topk(x, k).indices) along the last axis. ``tie_rule="torch"`` is
+    the reference's torch.topk (ties resolved by torch's CPU algorithm);
+    ``"smallest_index"`` breaks ties at the k-th value towards smaller indices
+    (the rule of the device top-k kernel)."""
+    if tie_rule == "torch":
+        return torch.sort(torch.topk(x, k=k, dim=-1).indices, dim=-1).values
+    from .select import topk_sorted
+    x2 = x.reshape(-1, x.shape[-1]).detach().numpy()
+    return torch.from_numpy(topk_sorted(x2, k)).reshape(x.shape[:-1] + (k,))
+
+
+def self_attention(attn, hidden, mask, active_heads, cumulative, kn: LayerKnobs, tie_rule="torch"):
     """One SpAtten self-attention (spatten_bert.py:48-164). Returns
     (full_context [B,S,H*D], next_heads, next_tokens, cumulative, info)."""
     n_heads = attn.num_attention_heads
@@ -137,8 +149,11 @@ def self_attention(attn, hidden, mask, active_heads, cumulative, kn: LayerKnobs)
             else kn.head_prune_num
         if cur > prune:
             keep = max(1, cur - prune)
-            _, ti = torch.topk(head_imp, k=keep)
-            next_heads = torch.sort(heads[ti]).values
+            if tie_rule == "torch":
+                _, ti = torch.topk(head_imp, k=keep)
+                next_heads = torch.sort(heads[ti]).values
+            else:
+                next_heads = heads[_topk_sorted(head_imp, keep, tie_rule)]
     if cumulative is None:
         cumulative = tok
     else:
@@ -150,8 +165,7 @@ def self_attention(attn, hidden, mask, active_heads, cumulative, kn: LayerKnobs)
             if kn.token_keep_ratio is not None else kn.token_prune_num
         if seq_len > prune:
             keep = max(1, seq_len - prune)
-            _, ti = torch.topk(cumulative, k=keep, dim=1)
-            next_tokens = torch.sort(ti, dim=1).values
+            next_tokens = _topk_sorted(cumulative, keep, tie_rule)
     ctx = ctx.permute(0, 2, 1, 3).contiguous()
     full = torch.zeros(bs, seq_len, n_heads, d, dtype=hidden.dtype)
     full[:, :, heads, :] = ctx
@@ -159,10 +173,11 @@ def self_attention(attn, hidden, mask, active_heads, cumulative, kn: LayerKnobs)
 
 
 @torch.no_grad()
-def spatten_bert_forward(model, input_ids, attention_mask=None, knobs=None):
+def spatten_bert_forward(model, input_ids, attention_mask=None, knobs=None, tie_rule="torch"):
     """Cascade forward (module.py:40-99). ``knobs``: list of LayerKnobs (one
-    per layer) or a single LayerKnobs for all layers. Returns a dict with the
-    last hidden state and the per-layer pruning decisions."""
+    per layer) or a single LayerKnobs for all layers; ``tie_rule`` see
+    ``_topk_sorted``. Returns a dict with the last hidden state and the
+    per-layer pruning decisions."""
     layers = model.encoder.layer
     if knobs is None:
         knobs = LayerKnobs()
@@ -181,7 +196,7 @@ def spatten_bert_forward(model, input_ids, attention_mask=None, knobs=None):
             if cumulative is not None:
                 cumulative = torch.gather(cumulative, 1, tokens)
         full, heads_n, tokens_n, cumulative, info = self_attention(
-            layer.attention.self, hidden, mask, heads, cumulative, knobs[i])
+            layer.attention.self, hidden, mask, heads, cumulative, knobs[i], tie_rule)
         att_out = layer.attention.output(full, hidden)
         hidden = layer.output(layer.intermediate(att_out), att_out)
         heads, tokens = heads_n, tokens_n

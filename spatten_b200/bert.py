@@ -14,6 +14,10 @@ Same API as the reference:
   (module.py:12-34), on the device gather kernel.
 * ``patch_bert(model)`` does the module swap and the binding in one call.
 
+With the batch sharded over ranks (``process_group`` on every attention
+module), the head importance is all-reduced before the head top-k, so all
+ranks keep the same heads as a single process would on the whole batch.
+
 Knobs (per attention module): ``enable_head_prune``/``head_prune_num``,
 ``enable_token_prune``/``token_prune_num``, ``enable_v_prune``/``v_prune_num``,
 ``enable_prog_quant``/``quant_threshold`` as in the reference, plus the ratio
@@ -98,6 +102,9 @@ class SpattenBertSelfAttention(BertSelfAttention):
         self.head_keep_ratio = None
         self.token_keep_ratio = None
         self.v_prune_threshold = None
+        # batch sharded over ranks: all-reduce head importance over this group
+        # (the reference's head decision is batch-global)
+        self.process_group = None
         # diagnostics of the last forward
         self.last_refetch = None
         self.last_head_importance = None
@@ -166,7 +173,11 @@ class SpattenBertSelfAttention(BertSelfAttention):
             self.last_refetch = r.refetch
         else:
             r = prog_attn(q, k, v, mode=N.MODE_DENSE, **common)
-        head_imp = r.head_abs_sum / float(B * S * d)
+        if self.process_group is not None:
+            from .distributed import allreduce_head_importance
+            head_imp = allreduce_head_importance(r.head_abs_sum, B * S * d, self.process_group)
+        else:
+            head_imp = r.head_abs_sum / float(B * S * d)
         self.last_head_importance = head_imp
         hp, tp = self._prune_counts(cur, S)
         next_heads = heads
@@ -219,7 +230,9 @@ def spatten_encoder_forward(self, hidden_states, attention_mask=None, **kwargs):
 def patch_bert(model, **knobs):
     """Swap every layer's self-attention for SpattenBertSelfAttention (weights
     carried over with load_state_dict, spatten_bert_ultimate.py:294-298),
-    bind the cascade encoder loop (:300) and set ``knobs`` on every layer."""
+    bind the cascade encoder loop (:300) and set ``knobs`` on every layer.
+    ``process_group=`` makes the head decision global over a batch sharded
+    across the group's ranks."""
     for i, layer in enumerate(model.encoder.layer):
         old = layer.attention.self
         new = SpattenBertSelfAttention(model.config)

@@ -110,8 +110,10 @@ static int fill_params(const spatten_prog_attn_args* a, spatten::AttnParams& p) 
   if (!a) return fail(SPATTEN_ERR_INVALID, "prog_attn: null args");
   if (a->mode < 0 || a->mode > 2) return fail(SPATTEN_ERR_INVALID, "prog_attn: bad mode %d", a->mode);
   if (a->dtype < 0 || a->dtype > 2) return fail(SPATTEN_ERR_INVALID, "prog_attn: bad dtype %d", a->dtype);
-  if (a->dtype == SPATTEN_DTYPE_F32)
-    return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: fp32 tensors are not supported (use f16/bf16)");
+  if (a->dtype == SPATTEN_DTYPE_F32 && a->mode == SPATTEN_MODE_COMPAT)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: COMPAT takes f16/bf16 planes");
+  if (a->dtype == SPATTEN_DTYPE_F32 && a->N > spatten::f32_max_keys())
+    return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: fp32 supports N <= %d keys", spatten::f32_max_keys());
   if (a->Z < 1 || a->H < 1 || a->Hkv < 1 || a->M < 1 || a->N < 1)
     return fail(SPATTEN_ERR_INVALID, "prog_attn: empty shape Z=%d H=%d Hkv=%d M=%d N=%d", a->Z,
                 a->H, a->Hkv, a->M, a->N);

@@ -48,6 +48,10 @@ int tc_tile_rows();
 cudaError_t launch_prog_attn_tc(const AttnParams& p, cudaStream_t st);
 // mma.sync kernel (COMPAT mode)
 cudaError_t launch_prog_attn_mma(const AttnParams& p, cudaStream_t st);
+// SIMT kernel for fp32 tensors (QUANT and DENSE modes, N <= f32_max_keys())
+int f32_tile_rows();
+int f32_max_keys();
+cudaError_t launch_prog_attn_f32(const AttnParams& p, cudaStream_t st);
 // device error word written by a kernel whose bounded wait ran out
 cudaError_t read_device_error(unsigned int* code, bool reset);
 

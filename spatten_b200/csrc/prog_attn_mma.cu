@@ -646,12 +646,16 @@ cudaError_t launch_prog_attn_mma(const AttnParams& p, cudaStream_t st) {
   return cudaErrorInvalidValue;
 }
 
-// QUANT and DENSE run on the tcgen05 kernel; the reference-compatible float
-// planes (COMPAT) on the warp-level kernel above.
-int attn_tile_rows(const AttnParams& p) { return p.mode == kCompat ? BM : tc_tile_rows(); }
+// QUANT and DENSE run on the tcgen05 kernel (fp16/bf16) or the fp32 kernel;
+// the reference-compatible float planes (COMPAT) on the warp-level kernel above.
+int attn_tile_rows(const AttnParams& p) {
+  if (p.mode == kCompat) return BM;
+  return p.dtype == kF32 ? f32_tile_rows() : tc_tile_rows();
+}
 
 cudaError_t launch_prog_attn(const AttnParams& p, cudaStream_t st, int) {
   if (p.mode == kCompat) return launch_prog_attn_mma(p, st);
+  if (p.dtype == kF32) return launch_prog_attn_f32(p, st);
   return launch_prog_attn_tc(p, st);
 }
 

@@ -1,0 +1,60 @@
+"""Sharding over ranks (one process per GPU) and the importance all-reduces.
+
+The (batch, head) units of the attention kernel are independent, so work is
+partitioned without a collective on the data path. Two decisions of the
+cascade are not local, and each needs exactly one all-reduce:
+
+* Head pruning is batch-global in the reference: head importance is
+  ``context.abs().mean(dim=(0, 2, 3))`` over the whole batch
+  (spatten_bert.py:120-121). With the batch sharded, every rank all-reduces
+  its per-head sums of |context| and the element count, so that all ranks
+  take the same top-k and keep the same heads (``allreduce_head_importance``).
+* Token importance sums over heads (spatten_bert.py:136). With heads split
+  across ranks, every rank all-reduces its partial [B, S] sums before the
+  token top-k (``allreduce_token_importance``).
+
+Collectives go through ``torch.distributed`` (NCCL over NVLink on GPUs, gloo
+on the CPU for tests) on the current stream.
+"""
+import torch
+import torch.distributed as dist
+
+
+def world():
+    """(rank, world_size) of the default group, (0, 1) without one."""
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(), dist.get_world_size()
+    return 0, 1
+
+
+def shard_range(n, rank, world_size):
+    """Contiguous [start, stop) of ``n`` units for ``rank`` (sizes differ by <= 1)."""
+    base, extra = divmod(n, world_size)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def shard_batch(x, rank=None, world_size=None, dim=0):
+    """This rank's slice of ``x`` along ``dim`` (the batch)."""
+    if rank is None or world_size is None:
+        rank, world_size = world()
+    a, b = shard_range(x.shape[dim], rank, world_size)
+    return x.narrow(dim, a, b - a)
+
+
+def allreduce_head_importance(head_abs_sum, count, group=None):
+    """Global mean |context| per head from per-rank sums.
+
+    ``head_abs_sum`` [H] fp32: this rank's sum of |context| per head;
+    ``count``: this rank's number of summed elements per head (B_local*S*D).
+    Returns the batch-global mean, identical on every rank."""
+    buf = torch.cat([head_abs_sum.double().reshape(-1),
+                     torch.tensor([float(count)], dtype=torch.float64, device=head_abs_sum.device)])
+    dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
+    return (buf[:-1] / buf[-1]).to(torch.float32)
+
+
+def allreduce_token_importance(tok, group=None):
+    """Sum the per-rank partial token importance [B, S] (heads split across ranks)."""
+    dist.all_reduce(tok, op=dist.ReduceOp.SUM, group=group)
+    return tok

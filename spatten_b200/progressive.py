@@ -127,8 +127,8 @@ def prog_attn(q, k0, v, *, mode, k1=None, q_scale=None, k_scale=None, sm_scale=N
     k14 = None if k1 is None else _as4d(k1, "k1")
     Z, H, M, D = q4.shape
     Hkv, Nk = v4.shape[1], v4.shape[2]
-    if v.dtype not in (torch.float16, torch.bfloat16):
-        raise TypeError(f"v: dtype {v.dtype} (need float16 or bfloat16)")
+    if v.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        raise TypeError(f"v: dtype {v.dtype} (need float16, bfloat16 or float32)")
     if k14 is not None and k14.stride() != k04.stride():
         raise ValueError("k planes must share strides")
     if out is None:

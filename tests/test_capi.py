@@ -75,7 +75,7 @@ def test_workspace_size_matches_partials():
 
 
 @pytest.mark.parametrize("field,value,code", [
-    ("mode", 7, 1), ("dtype", 9, 1), ("dtype", 2, 3), ("D", 96, 3), ("M", 0, 1), ("N", 0, 1),
+    ("mode", 7, 1), ("dtype", 9, 1), ("D", 96, 3), ("M", 0, 1), ("N", 0, 1),
     ("Hkv", 3, 1), ("q", 0, 1), ("k1", 0, 1), ("k0", (1 << 20) + 8, 1), ("v_sn", 65, 1),
     ("q_sm", -64, 1),
 ])
@@ -92,6 +92,14 @@ def test_prog_attn_requires_workspace():
     a = _args(N, tok_out=1 << 21)
     assert N.lib.spatten_prog_attn(a, None, 0, None) == N.ERR_INVALID
     assert b"workspace" in N.lib.spatten_last_error()
+
+
+def test_fp32_limits():
+    from spatten_b200 import _native as N
+    a = _args(N, dtype=N.DTYPE_F32, mode=N.MODE_COMPAT, tile_m=32, tile_n=32)
+    assert N.lib.spatten_prog_attn(a, None, 0, None) == N.ERR_UNSUPPORTED
+    a = _args(N, dtype=N.DTYPE_F32, N=9000)
+    assert N.lib.spatten_prog_attn(a, None, 0, None) == N.ERR_UNSUPPORTED
 
 
 def test_compat_tile_validation():

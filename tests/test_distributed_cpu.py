@@ -1,0 +1,73 @@
+"""Multi-rank host logic on CPU ranks (gloo, world size 2): batch sharding
+and the head / token importance all-reduces give every rank the decision a
+single process takes on the whole batch (spatten_bert.py:120-130, 136-150)."""
+import os
+import socket
+
+import numpy as np
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, ctx, q):
+    import torch.distributed as dist
+    from spatten_b200 import distributed as sd
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        local = sd.shard_batch(ctx, rank, world)          # [B_local, H, S, D]
+        B, H, S, D = local.shape
+        head = sd.allreduce_head_importance(local.abs().sum(dim=(0, 2, 3)), B * S * D)
+        # heads split (whole batch on every rank): partial sums over my heads
+        tok_part = ctx[:, rank::world].abs().sum(dim=(1, 3))
+        tok = sd.allreduce_token_importance(tok_part.clone())
+        q.put((rank, head.numpy(), tok.numpy(), (B, sd.shard_range(ctx.shape[0], rank, world))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_shard_range_covers_everything():
+    from spatten_b200.distributed import shard_range
+    for n in (1, 5, 8, 33):
+        for w in (1, 2, 3, 8):
+            spans = [shard_range(n, r, w) for r in range(w)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            assert max(b - a for a, b in spans) - min(b - a for a, b in spans) <= 1
+
+
+def test_gloo_two_ranks_importance_allreduce():
+    g = torch.Generator().manual_seed(0)
+    ctx = torch.randn(5, 4, 7, 8, generator=g)
+    world = 2
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    port = _free_port()
+    procs = [mpc.Process(target=_worker, args=(r, world, port, ctx, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # single-process decisions on the whole batch
+    head_ref = ctx.abs().mean(dim=(0, 2, 3)).numpy()
+    for rank, head, tok, _ in out:
+        np.testing.assert_allclose(head, head_ref, rtol=1e-6)
+        # same kept heads on every rank
+        assert np.array_equal(np.sort(np.argsort(-head)[:3]), np.sort(np.argsort(-head_ref)[:3]))
+    sizes = sorted(o[3][0] for o in out)
+    assert sizes == [2, 3]
+    # token importance: partial sums over each rank's heads add up to all heads
+    expect = ctx.abs().sum(dim=(1, 3)).numpy()
+    for _, _, tok, _ in out:
+        np.testing.assert_allclose(tok, expect, rtol=1e-5)
