@@ -41,13 +41,15 @@ using namespace sm100;
 
 constexpr int BM = 128;        // query rows per CTA (= TMEM lanes)
 constexpr int BN = 64;         // keys per tile
-constexpr int kThreads = 256;  // 8 warps
+constexpr int kSoftWarps = 8;  // two per TMEM lane quarter, 32 columns each
+constexpr int kSoftThreads = kSoftWarps * 32;
+constexpr int kThreads = 384;  // 12 warps
 constexpr int kNStg = 3;       // packed-plane staging stages (QUANT)
 constexpr int kNExp = 2;       // K operand stages
 constexpr int kNV = 2;         // V stages
 constexpr int kNP = 2;         // P buffers
-constexpr uint32_t kTmemCols = 256;
-constexpr int kWarpTma = 4, kWarpMma = 5, kWarpExp = 6;
+constexpr int kCsCols = 16;    // N of the column-sum MMA (16 identical columns)
+constexpr int kWarpTma = 8, kWarpMma = 9, kWarpExp = 10;
 
 enum Mode : int { kQuant = 0, kDense = 1 };
 
@@ -69,17 +71,23 @@ struct Layout {
   static constexpr int kStgBytes = (MODE == kQuant) ? BN * D : 0;  // msb + lsb packed
   static constexpr int kVBytes = (D / 64) * BN * 128;   // V stage (MN-major blocks of 64 dims)
   static constexpr int kPBytes = BM * 128;              // P stage (64 keys x 2 B per row)
+  static constexpr int kOnesBytes = 2 * kCsCols * 128;  // ones [16][128] (B of the column sums)
+  // tensor memory: S buffers [0, 2*BN), O [2*BN, 2*BN+D), column sums after O
+  static constexpr int kColO = 2 * BN;
+  static constexpr int kColCs = 2 * BN + D;
+  static constexpr uint32_t kTmemCols = (kColCs + 2 * kCsCols) <= 256 ? 256 : 512;
   static constexpr int oQ = 0;
   static constexpr int oK = oQ + kQBytes;
   static constexpr int oV = oK + kNExp * kKBytes;
   static constexpr int oP = oV + kNV * kVBytes;
   static constexpr int oStg = oP + kNP * kPBytes;       // 1024-aligned so far
-  static constexpr int oKs = oStg + kNStg * kStgBytes;  // float [kNExp][BN] key scale
+  static constexpr int oOnes = oStg + kNStg * kStgBytes;  // 1024-aligned
+  static constexpr int oKs = oOnes + kOnesBytes;        // float [kNExp][BN] key scale
   static constexpr int oKb = oKs + kNExp * BN * 4;      // float [kNExp][BN] key bias * log2e
-  static constexpr int oCs = oKb + kNExp * BN * 4;      // float [2][4][BN] column sums
-  static constexpr int oHs = oCs + 2 * 4 * BN * 4;      // float [4]
-  static constexpr int oBar = oHs + 16;                 // mbarriers
-  static constexpr int kNumBars = 2 * kNStg + 2 * kNExp + 2 * 2 + 2 * kNP + 2 * kNV + 3;
+  static constexpr int oSt = oKb + kNExp * BN * 4;      // float [2 (m,l)][2 halves][BM] row statistics
+  static constexpr int oHs = oSt + 2 * 2 * BM * 4;      // float [kSoftWarps]
+  static constexpr int oBar = oHs + 4 * kSoftWarps;     // mbarriers
+  static constexpr int kNumBars = 2 * kNStg + 2 * kNExp + 2 * 2 + 2 * kNP + 2 * kNV + 2 * 2 + 3;
   static constexpr int oTmem = oBar + kNumBars * 8;
   static constexpr int oFlag = oTmem + 4;  // int abort, int decision
   static constexpr int kBytes = oFlag + 16;
@@ -97,6 +105,8 @@ struct Bars {
   uint64_t* p_empty;
   uint64_t* v_full;
   uint64_t* v_empty;
+  uint64_t* cs_full;
+  uint64_t* cs_empty;
   uint64_t* q_ready;
   uint64_t* dec_ready;
   uint64_t* o_full;
@@ -152,6 +162,8 @@ struct Cta {
     b.p_empty = bar; bar += kNP;
     b.v_full = bar; bar += kNV;
     b.v_empty = bar; bar += kNV;
+    b.cs_full = bar; bar += 2;
+    b.cs_empty = bar; bar += 2;
     b.q_ready = bar++;
     b.dec_ready = bar++;
     b.o_full = bar++;
@@ -172,22 +184,24 @@ struct Cta {
     }
     for (int i = 0; i < kNExp; ++i) {
       mbar_init(&b.k_full[i], MODE == kQuant ? 2 : 3);
-      mbar_init(&b.k_empty[i], 1 + 4);
+      mbar_init(&b.k_empty[i], 1 + kSoftWarps);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&b.s_full[i], 1);
-      mbar_init(&b.s_empty[i], 4);
+      mbar_init(&b.s_empty[i], kSoftWarps);
+      mbar_init(&b.cs_full[i], 1);
+      mbar_init(&b.cs_empty[i], 4);
     }
     for (int i = 0; i < kNP; ++i) {
-      mbar_init(&b.p_full[i], 4);
+      mbar_init(&b.p_full[i], kSoftWarps);
       mbar_init(&b.p_empty[i], 1);
     }
     for (int i = 0; i < kNV; ++i) {
       mbar_init(&b.v_full[i], 1);
       mbar_init(&b.v_empty[i], 1);
     }
-    mbar_init(b.q_ready, 4);
-    mbar_init(b.dec_ready, 4);
+    mbar_init(b.q_ready, kSoftWarps);
+    mbar_init(b.dec_ready, kSoftWarps);
     mbar_init(b.o_full, 1);
     *abort = 0;
     *decision = 0;
@@ -365,10 +379,12 @@ struct Cta {
     constexpr uint32_t idesc_s = (MODE == kQuant) ? instr_desc(2, 1, 0, 0, BM, BN)
                                                   : instr_desc(1, ab16, 0, 0, BM, BN);
     constexpr uint32_t idesc_pv = instr_desc(1, ab16, 0, 1, BM, D);
+    constexpr uint32_t idesc_cs = instr_desc(1, ab16, 1, 0, BM, kCsCols);
+    const bool want_tok = p.tok_partial != nullptr;
     const uint32_t qaddr = smem_u32(sm + L::oQ);
     if (!mbar_wait(b.q_ready, 0, kErrMma | 1, abort)) return;
     tc_fence_after();
-    uint32_t t = 0, tp = 0, tv = 0;
+    uint32_t t = 0, tv = 0;
     int any = 0;
     bool first_pv = true;
     for (int pass = 0; pass < 3; ++pass) {
@@ -401,9 +417,10 @@ struct Cta {
           mma_commit(&b.k_empty[es]);
           ++t;
         }
-        if (pass == 2 && j >= 1) {  // O += P_{j-1} V_{j-1}
-          const int pb = tp % kNP, vs = tv % kNV;
-          if (!mbar_wait(&b.p_full[pb], (tp / kNP) & 1, kErrMma | 5, abort)) { ok = false; break; }
+        if (pass == 2 && j >= 1) {  // O += P_jj V_jj, jj = j - 1
+          const int jj = j - 1;
+          const int pb = jj % kNP, vs = tv % kNV;
+          if (!mbar_wait(&b.p_full[pb], (jj / kNP) & 1, kErrMma | 5, abort)) { ok = false; break; }
           if (!mbar_wait(&b.v_full[vs], (tv / kNV) & 1, kErrMma | 6, abort)) { ok = false; break; }
           tc_fence_after();
           const uint32_t paddr = smem_u32(sm + L::oP + pb * L::kPBytes);
@@ -412,13 +429,33 @@ struct Cta {
           for (int kk = 0; kk < BN / 16; ++kk) {
             const uint64_t ad = smem_desc_sw128(paddr + kk * 32, 16, 1024);
             const uint64_t bd = smem_desc_sw128(vaddr + kk * 2048, BN * 128, 1024);
-            mma_f16(tmem + 2 * BN, ad, bd, idesc_pv, (first_pv && kk == 0) ? 0u : 1u);
+            mma_f16(tmem + L::kColO, ad, bd, idesc_pv, (first_pv && kk == 0) ? 0u : 1u);
           }
           first_pv = false;
-          mma_commit(&b.p_empty[pb]);
           mma_commit(&b.v_empty[vs]);
-          ++tp;
           ++tv;
+          const bool pair_end = (jj & 1) || jj == nt - 1;
+          if (!want_tok) {
+            mma_commit(&b.p_empty[pb]);
+          } else if (pair_end) {
+            // token importance of the pair's 128 keys: P'^T as an MN-major A
+            // operand (the two P buffers are its two 64-key blocks, LBO apart)
+            // times a [rows x 16] block of ones; K = the CTA's 128 query rows.
+            const int pi = jj >> 1, cb = pi & 1;
+            if (!mbar_wait(&b.cs_empty[cb], ((pi >> 1) & 1) ^ 1, kErrMma | 7, abort)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t p0 = smem_u32(sm + L::oP);
+            const uint32_t ones = smem_u32(sm + L::oOnes);
+#pragma unroll
+            for (int kk = 0; kk < BM / 16; ++kk) {
+              const uint64_t ad = smem_desc_sw128(p0 + kk * 2048, L::kPBytes, 1024);
+              const uint64_t bd = smem_desc_sw128(ones + (kk >> 2) * (kCsCols * 128) + (kk & 3) * 32, 16, 1024);
+              mma_f16(tmem + L::kColCs + cb * kCsCols, ad, bd, idesc_cs, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(&b.cs_full[cb]);
+            if (jj & 1) mma_commit(&b.p_empty[0]);  // the pair's even tile
+            mma_commit(&b.p_empty[pb]);
+          }
         }
         if (pass != 2 && j == nt - 1) break;
       }
@@ -435,21 +472,22 @@ struct Cta {
 
   // -------------------------------------------------------------- softmax
   SPATTEN_DEV void softmax_role();
-  SPATTEN_DEV void load_q_row(int r, bool valid);
+  SPATTEN_DEV void load_q_row(int r, bool valid, int hf);
 };
 
-// Q row r -> Q' operand (first D bytes for QUANT, 2D bytes for DENSE), zeros if invalid.
+// Q row r -> Q' operand (first D bytes for QUANT, 2D bytes for DENSE), zeros
+// if invalid; the two softmax threads of a row load alternate halves.
 template <int MODE, typename T, int D>
-SPATTEN_DEV void Cta<MODE, T, D>::load_q_row(int r, bool valid) {
+SPATTEN_DEV void Cta<MODE, T, D>::load_q_row(int r, bool valid, int hf) {
   const int row = m0 + r;
   uint8_t* base = sm + L::oQ;
   const int sw = r & 7;
   const int esz = (MODE == kQuant) ? 1 : (int)sizeof(T);
-  const int bytes = D * esz;  // q row bytes
+  constexpr int kChunks = D * ((MODE == kQuant) ? 1 : (int)sizeof(T)) / 16;
   const uint8_t* src = static_cast<const uint8_t*>(p.q) +
                        ((int64_t)z * p.q_sz + (int64_t)h * p.q_sh + (int64_t)row * p.q_sm) * esz;
   const bool al16 = ((reinterpret_cast<uintptr_t>(src)) & 15) == 0;
-  for (int c = 0; c < bytes / 16; ++c) {
+  for (int c = hf * (kChunks / 2); c < (hf + 1) * (kChunks / 2); ++c) {
     uint4 v = make_uint4(0, 0, 0, 0);
     if (valid) {
       if (al16) {
@@ -467,17 +505,27 @@ SPATTEN_DEV void Cta<MODE, T, D>::load_q_row(int r, bool valid) {
 
 template <int MODE, typename T, int D>
 SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
-  const int r = threadIdx.x;  // row within the tile = TMEM lane
-  const int warp = r >> 5, lane = r & 31;
+  constexpr int HC = BN / 2;        // columns per softmax thread and tile
+  const int tid = threadIdx.x;      // 0 .. kSoftThreads-1
+  const int warp = tid >> 5, lane = tid & 31;
+  const int qd = warp & 3;          // TMEM lane quarter
+  const int hf = warp >> 2;         // which 32 of the tile's 64 columns
+  const int r = qd * 32 + lane;     // row within the tile = TMEM lane
+  const int c0 = hf * HC;
   const int row = m0 + r;
   const bool valid = row < p.M;
-  const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's lane quarter
+  const uint32_t tl = tmem + ((uint32_t)(qd * 32) << 16);
   float c2 = 0.f;
   if (valid) {
     c2 = (MODE == kQuant) ? p.q_scale[((int64_t)z * p.H + h) * p.M + row] * p.sm_scale * kLog2e
                           : p.sm_scale * kLog2e;
   }
-  load_q_row(r, valid);
+  {  // ones block: B operand of the column-sum MMA (every element 1.0)
+    const uint32_t one2 = pack2<T>(1.f, 1.f);
+    uint4* ob = reinterpret_cast<uint4*>(sm + L::oOnes);
+    for (int i = tid; i < L::kOnesBytes / 16; i += kSoftThreads) ob[i] = make_uint4(one2, one2, one2, one2);
+  }
+  load_q_row(r, valid, hf);
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) mbar_arrive(b.q_ready);
@@ -489,14 +537,15 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
   const int shift = p.N - p.M;
   const float* ksm = reinterpret_cast<const float*>(sm + L::oKs);
   const float* kbm = reinterpret_cast<const float*>(sm + L::oKb);
+  float* stm = reinterpret_cast<float*>(sm + L::oSt);  // [2][2][BM]
 
   uint32_t t = 0;
   bool alive = true;
 
-  // Tile t's scores (64 columns) from TMEM, as log2-domain floats with the
-  // key scale, the bias and the masks applied. With `dump`, the integer
-  // scores also go to score_out. On an abort the tile is skipped (alive=false).
-  auto scores = [&](int j, float (&s)[BN], int32_t* dump) {
+  // This thread's 32 scores of tile j (columns c0..c0+31 of the 64), as
+  // log2-domain floats with key scale, bias and masks applied. With `dump`,
+  // the integer scores also go to score_out.
+  auto scores = [&](int j, float (&s)[HC], int32_t* dump) {
     const int sb = t & 1, es = t % kNExp;
     const uint32_t tt = t++;
     if (!alive) return;
@@ -504,31 +553,27 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
     tc_fence_after();
     uint32_t* u = reinterpret_cast<uint32_t*>(s);
     {
-      uint32_t r0[32], r1[32];
-      tmem_ld32(tl + sb * BN, r0);
-      tmem_ld32(tl + sb * BN + 32, r1);
+      uint32_t r0[32];
+      tmem_ld32(tl + sb * BN + c0, r0);
       tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        u[i] = r0[i];
-        u[32 + i] = r1[i];
-      }
+      for (int i = 0; i < 32; ++i) u[i] = r0[i];
     }
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&b.s_empty[sb]);
-    const int n0 = j * BN;
+    const int n0 = j * BN + c0;
     if (dump && valid) {
-      for (int i = 0; i < BN; ++i)
+      for (int i = 0; i < HC; ++i)
         if (n0 + i < p.N) dump[(int64_t)row * p.N + n0 + i] = (int32_t)u[i];
     }
     if (!mbar_wait(&b.k_full[es], (tt / kNExp) & 1, kErrSoftmax | 2, abort)) { alive = false; return; }
-    const float* ks = ksm + es * BN;
-    const float* kb = kbm + es * BN;
+    const float* ks = ksm + es * BN + c0;
+    const float* kb = kbm + es * BN + c0;
     if (MODE == kQuant) {
       const f2 c22 = pack_f2(c2, c2);
 #pragma unroll
-      for (int i = 0; i < BN; i += 4) {
+      for (int i = 0; i < HC; i += 4) {
         const float4 k4 = *reinterpret_cast<const float4*>(ks + i);
         const float x0 = i2f_exact(u[i]) - kMagic, x1 = i2f_exact(u[i + 1]) - kMagic;
         const float x2 = i2f_exact(u[i + 2]) - kMagic, x3 = i2f_exact(u[i + 3]) - kMagic;
@@ -539,11 +584,11 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < BN; ++i) s[i] = __uint_as_float(u[i]) * c2;
+      for (int i = 0; i < HC; ++i) s[i] = __uint_as_float(u[i]) * c2;
     }
     if (key_bias) {
 #pragma unroll
-      for (int i = 0; i < BN; i += 4) {
+      for (int i = 0; i < HC; i += 4) {
         const float4 k4 = *reinterpret_cast<const float4*>(kb + i);
         s[i] += k4.x;
         s[i + 1] += k4.y;
@@ -554,87 +599,123 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
     __syncwarp();
     if (lane == 0) mbar_arrive(&b.k_empty[es]);
     if (gen_bias && valid) {
-      for (int i = 0; i < BN; ++i)
+      for (int i = 0; i < HC; ++i)
         if (n0 + i < p.N) s[i] += __ldg(brow + (int64_t)(n0 + i) * p.b_sn) * kLog2e;
     }
     // keys past N and, with the causal mask, keys after the row's diagonal:
     // only tiles that reach them pay for the per-element test
     int lim = p.N - n0;
     if (p.causal) lim = min(lim, row + shift + 1 - n0);
-    if (lim < BN) {
+    if (lim < HC) {
 #pragma unroll
-      for (int i = 0; i < BN; ++i)
+      for (int i = 0; i < HC; ++i)
         if (i >= lim) s[i] = -INFINITY;
     }
   };
 
-  // Online row statistics over one tile. Eight independent max / sum chains
-  // keep the dependent-latency per tile short.
-  auto stats = [&](const float (&s)[BN], float& m, float& l) {
-    float mx[8];
+  // Online statistics of this thread's half row over one tile (four
+  // independent max / sum chains).
+  auto stats = [&](const float (&s)[HC], float& m, float& l) {
+    float mx[4];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) mx[k] = s[k];
+    for (int k = 0; k < 4; ++k) mx[k] = s[k];
 #pragma unroll
-    for (int i = 8; i < BN; i += 8)
+    for (int i = 4; i < HC; i += 4)
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], s[i + k]);
-    const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      for (int k = 0; k < 4; ++k) mx[k] = fmaxf(mx[k], s[i + k]);
+    const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
     const float mn = fmaxf(m, tmax);
     if (mn == -INFINITY) return;
     const f2 nm2 = pack_f2(-mn, -mn);
-    f2 acc[4];
+    f2 acc[2];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < 2; ++k) {
       float a0, a1;
       unpack_f2(fadd2(pack_f2(s[2 * k], s[2 * k + 1]), nm2), a0, a1);
       acc[k] = pack_f2(fast_exp2(a0), fast_exp2(a1));
     }
 #pragma unroll
-    for (int i = 8; i < BN; i += 8)
+    for (int i = 4; i < HC; i += 4)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < 2; ++k) {
         float a0, a1;
         unpack_f2(fadd2(pack_f2(s[i + 2 * k], s[i + 2 * k + 1]), nm2), a0, a1);
         acc[k] = fadd2(acc[k], pack_f2(fast_exp2(a0), fast_exp2(a1)));
       }
-    float t0, t1, t2, t3, t4, t5, t6, t7;
+    float t0, t1, t2, t3;
     unpack_f2(acc[0], t0, t1);
     unpack_f2(acc[1], t2, t3);
-    unpack_f2(acc[2], t4, t5);
-    unpack_f2(acc[3], t6, t7);
-    const float sum = ((t0 + t1) + (t2 + t3)) + ((t4 + t5) + (t6 + t7));
-    l = l * fast_exp2(m - mn) + sum;
+    l = l * fast_exp2(m - mn) + ((t0 + t1) + (t2 + t3));
     m = mn;
   };
 
-  float s[BN];
+  // Both softmax threads of a row end up with the statistics of the whole
+  // row: half 0 then half 1, in that order, on both threads.
+  auto combine = [&](float& m, float& l) {
+    stm[(0 * 2 + hf) * BM + r] = m;
+    stm[(1 * 2 + hf) * BM + r] = l;
+    named_sync(1, kSoftThreads);
+    const float ma = stm[(0 * 2 + 0) * BM + r], la = stm[(1 * 2 + 0) * BM + r];
+    const float mb = stm[(0 * 2 + 1) * BM + r], lb = stm[(1 * 2 + 1) * BM + r];
+    named_sync(1, kSoftThreads);
+    const float mn = fmaxf(ma, mb);
+    if (mn == -INFINITY) {
+      m = mn;
+      l = 0.f;
+      return;
+    }
+    m = mn;
+    l = la * fast_exp2(ma - mn) + lb * fast_exp2(mb - mn);
+  };
+
+  const bool want_tok = p.tok_partial != nullptr;
+  float* tokp = want_tok ? p.tok_partial + (((int64_t)z * p.H + h) * p.mtiles + mt) * p.N : nullptr;
+  // column sums of tile pair pi (128 keys) from TMEM; warps of half 0 cover
+  // the 128 lanes = keys
+  auto read_pair = [&](int pi) {
+    const int cb = pi & 1;
+    if (!alive) return;
+    if (!mbar_wait(&b.cs_full[cb], (pi >> 1) & 1, kErrSoftmax | 5, abort)) { alive = false; return; }
+    tc_fence_after();
+    uint32_t v;
+    tmem_ld1(tl + L::kColCs + cb * kCsCols, v);
+    tmem_wait_ld();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&b.cs_empty[cb]);
+    const int key = pi * 2 * BN + qd * 32 + lane;
+    if (key < p.N) tokp[key] = __uint_as_float(v);
+  };
+
+  float s[HC];
   float m_run = -INFINITY, l_run = 0.f;  // statistics of the scores in use
   float mf = -INFINITY, lf = 0.f;        // statistics of the full score (pass 1b)
   bool flag = false, warp_any = false;
   int any = 0;
-  const bool want_tok = p.tok_partial != nullptr;
-  float* tokp = want_tok ? p.tok_partial + (((int64_t)z * p.H + h) * p.mtiles + mt) * p.N : nullptr;
-  float* cs = reinterpret_cast<float*>(sm + L::oCs);
   const float vthr = p.v_thr;
   int32_t* dump = (MODE == kQuant && p.score_out)
                       ? p.score_out + ((int64_t)z * p.H + h) * p.M * (int64_t)p.N
                       : nullptr;
   f2 inv2 = pack_f2(0.f, 0.f), mn2 = pack_f2(0.f, 0.f);
+  int pairs_read = 0;
+  const int npairs = (nt + 1) / 2;
   // One loop over the passes keeps a single copy of the tile code:
   //   pass 0 statistics of the MSB (QUANT) / only (DENSE) score
   //   pass 1 statistics of the full score of refetched rows (QUANT, if any)
-  //   pass 2 P, V prune, P -> shared memory, column sums
+  //   pass 2 P, V prune, P -> shared memory (P.V and the column sums run on
+  //          the tensor cores)
   for (int pass = 0; pass < 3; ++pass) {
     if (pass == 1) {
+      combine(m_run, l_run);
       // ---- decide the refetch, build Q'
       if (MODE == kQuant) {
         flag = alive && valid && __frcp_rn(l_run) < p.refetch_thr;
-        // Q' bytes [D, 2D): q8 for a refetched row, zeros otherwise
+        // Q' bytes [D, 2D): q8 for a refetched row, zeros otherwise (each
+        // thread of the row copies half of the chunks)
         uint8_t* base = sm + L::oQ;
         const int sw = r & 7;
 #pragma unroll
-        for (int c = 0; c < D / 16; ++c) {
+        for (int c = hf * (D / 32); c < (hf + 1) * (D / 32); ++c) {
           const int src_off = 16 * c, dst_off = D + 16 * c;
           const uint4 v = *reinterpret_cast<const uint4*>(base + (src_off >> 7) * (BM * 128) + r * 128 +
                                                           ((((src_off >> 4) & 7) ^ sw) << 4));
@@ -645,16 +726,14 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
         fence_proxy_async_smem();
         uint32_t anyv;
         asm volatile(
-            "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n barrier.cta.red.or.pred p, 1, 128, q;\n"
+            "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n barrier.cta.red.or.pred p, 1, %2, q;\n"
             " selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(anyv)
-            : "r"((uint32_t)flag)
+            : "r"((uint32_t)flag), "n"(kSoftThreads)
             : "memory");
         any = (int)anyv;
-        if (r == 0) *decision = any;
-        if (p.refetch_out && valid) p.refetch_out[((int64_t)z * p.H + h) * p.M + row] = flag;
-      } else {
-        named_sync(1, 128);
+        if (tid == 0) *decision = any;
+        if (p.refetch_out && valid && hf == 0) p.refetch_out[((int64_t)z * p.H + h) * p.M + row] = flag;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(b.dec_ready);
@@ -662,9 +741,12 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
       warp_any = __any_sync(0xffffffffu, flag);
     }
     if (pass == 2) {
-      if (MODE == kQuant && any && flag) {
-        m_run = mf;
-        l_run = lf;
+      if (MODE == kQuant && any) {
+        combine(mf, lf);
+        if (flag) {
+          m_run = mf;
+          l_run = lf;
+        }
       }
       const float inv_l = (valid && m_run != -INFINITY && l_run > 0.f) ? 1.f / l_run : 0.f;
       const float mneg = (m_run == -INFINITY) ? 0.f : -m_run;
@@ -692,26 +774,27 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
       const int pb = j % kNP;
       if (alive) {
 #pragma unroll
-        for (int i = 0; i < BN; i += 2) {
+        for (int i = 0; i < HC; i += 2) {
           float a0, a1;
           unpack_f2(fadd2(pack_f2(s[i], s[i + 1]), mn2), a0, a1);
           unpack_f2(fmul2(pack_f2(fast_exp2(a0), fast_exp2(a1)), inv2), s[i], s[i + 1]);
         }
         if (vthr > 0.f) {
 #pragma unroll
-          for (int i = 0; i < BN; ++i) s[i] = s[i] < vthr ? 0.f : s[i];
+          for (int i = 0; i < HC; ++i) s[i] = s[i] < vthr ? 0.f : s[i];
         }
-        // P -> shared memory (A operand of P.V, K-major, 128B swizzle)
+        // P -> shared memory: A operand of P.V (K-major) and, read as an
+        // MN-major operand, of the column sums; 128B swizzle
         if (mbar_wait(&b.p_empty[pb], ((j / kNP) & 1) ^ 1, kErrSoftmax | 3, abort)) {
           uint8_t* prow = sm + L::oP + pb * L::kPBytes + r * 128;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
+          for (int c = 0; c < 4; ++c) {
             uint4 v;
             v.x = pack2<T>(s[8 * c], s[8 * c + 1]);
             v.y = pack2<T>(s[8 * c + 2], s[8 * c + 3]);
             v.z = pack2<T>(s[8 * c + 4], s[8 * c + 5]);
             v.w = pack2<T>(s[8 * c + 6], s[8 * c + 7]);
-            *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = v;
+            *reinterpret_cast<uint4*>(prow + (((hf * 4 + c) ^ (r & 7)) << 4)) = v;
           }
           fence_proxy_async_smem();
           __syncwarp();
@@ -720,52 +803,26 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
           alive = false;
         }
       }
-      if (want_tok) {
-        // column sums of this warp's 32 rows (P is in shared memory already, so
-        // s is reduced in place): reduce-scatter over the lanes, lane l ends
-        // with column (half*32 + l)
-        float* csb = cs + (j & 1) * 4 * BN + warp * BN;
-        if (!alive) {
-#pragma unroll
-          for (int i = 0; i < BN; ++i) s[i] = 0.f;
-        }
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          float* v = s + half * 32;
-#pragma unroll
-          for (int w = 16; w >= 1; w >>= 1) {
-            const bool up = lane & w;
-#pragma unroll
-            for (int i = 0; i < w; ++i) {
-              const float send = up ? v[i] : v[i + w];
-              const float keep = up ? v[i + w] : v[i];
-              v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
-            }
-          }
-          csb[half * 32 + lane] = v[0];
-        }
-        named_sync(1, 128);
-        if (r < BN && alive) {
-          const float* c0 = cs + (j & 1) * 4 * BN;
-          const int key = j * BN + r;
-          if (key < p.N) tokp[key] = ((c0[r] + c0[BN + r]) + c0[2 * BN + r]) + c0[3 * BN + r];
-        }
-      }
+      // column sums of the pair before last (its MMA had a pair's time to finish)
+      if (want_tok && hf == 0 && (j & 1) && j >= 3) read_pair(pairs_read++);
     }
   }
+  if (want_tok && hf == 0)
+    while (pairs_read < npairs) read_pair(pairs_read++);
 
-  // ---- epilogue: O (already normalised) from TMEM
+  // ---- epilogue: O (already normalised) from TMEM, this thread's half row
   if (!mbar_wait(b.o_full, 0, kErrSoftmax | 4, abort)) alive = false;
   tc_fence_after();
   float asum = 0.f;
   const int hslot = p.out_head_map ? p.out_head_map[h] : h;
   const bool out_ok = hslot >= 0 && hslot < p.out_head_slots;
-  T* orow = static_cast<T*>(p.out) + (int64_t)z * p.o_sz + (int64_t)hslot * p.o_sh + (int64_t)row * p.o_sm;
+  T* orow = static_cast<T*>(p.out) + (int64_t)z * p.o_sz + (int64_t)hslot * p.o_sh + (int64_t)row * p.o_sm +
+            hf * (D / 2);
   const bool out16 = (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
 #pragma unroll
-  for (int c = 0; c < D / 32; ++c) {
+  for (int c = 0; c < D / 64; ++c) {
     uint32_t o[32];
-    tmem_ld32(tl + 2 * BN + 32 * c, o);
+    tmem_ld32(tl + L::kColO + hf * (D / 2) + 32 * c, o);
     tmem_wait_ld();
     if (alive && valid) {
       uint32_t pk[16];
@@ -794,9 +851,12 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
     for (int off = 16; off > 0; off >>= 1) asum += __shfl_xor_sync(0xffffffffu, asum, off);
     float* hs = reinterpret_cast<float*>(sm + L::oHs);
     if (lane == 0) hs[warp] = asum;
-    named_sync(1, 128);
-    if (r == 0 && alive)
-      p.head_partial[((int64_t)z * p.H + h) * p.mtiles + mt] = ((hs[0] + hs[1]) + hs[2]) + hs[3];
+    named_sync(1, kSoftThreads);
+    if (tid == 0 && alive) {
+      float tot = 0.f;
+      for (int w = 0; w < kSoftWarps; ++w) tot += hs[w];
+      p.head_partial[((int64_t)z * p.H + h) * p.mtiles + mt] = tot;
+    }
   }
 }
 
@@ -812,14 +872,14 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(base + L::oTmem);
   if (threadIdx.x == 0) c.init_barriers();
   if (warp == kWarpMma) {
-    tmem_alloc(tslot, kTmemCols);
+    tmem_alloc(tslot, L::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   c.tmem = *tslot;
-  if (warp < 4) c.softmax_role();
+  if (warp < kSoftWarps) c.softmax_role();
   else if (warp == kWarpTma) c.tma_role();
   else if (warp == kWarpMma) c.mma_role();
   else c.expand_role();
@@ -827,7 +887,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
   __syncthreads();
   if (warp == kWarpMma) {
     tc_fence_after();
-    tmem_dealloc(c.tmem, kTmemCols);
+    tmem_dealloc(c.tmem, L::kTmemCols);
   }
 }
 
