@@ -334,6 +334,11 @@ struct Cta {
               Y[4 * i] = v.x; Y[4 * i + 1] = v.y; Y[4 * i + 2] = v.z; Y[4 * i + 3] = v.w;
             }
           }
+          // The stage is read through the generic proxy and refilled by the
+          // TMA (async proxy) as soon as it is released: without a proxy fence
+          // between the reads and the release, the next tile's bytes could land
+          // before these reads were performed (seen with two CTAs per SM).
+          fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(&b.stg_empty[s]);
         }
