@@ -15,6 +15,16 @@ N > 1 runs under torchrun, one rank per GPU; each rank processes its own
 batch of 8 (weak scaling, no collective on the data path). Rank 0 prints one
 JSON line. ``--impl reference`` times the CPU restatement of the op (the
 reference has no GPU path for it) on rank 0 over a bounded sample.
+
+Besides the op's throughput the line carries: the HBM GB/s of the attention
+launch; a roofline against the measured tensor peak plus the launch's time
+floor (slowest of HBM bytes, int8 + fp16 tensor work and MUFU exp2, with the
+int8 and exp2 rates measured here); the end-to-end rate through the public
+API with pinned host buffers (uploads and downloads overlap the previous /
+next step's compute on their own streams); and the BERT-base SpAtten forward
+in ms per batch (fp16 B32 S512 sharded over the ranks, and fp32 B1 S128 --
+the reference's CPU configuration, which the reference arm times on the host
+cores).
 """
 import argparse
 import json
@@ -46,6 +56,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seq", type=int, default=S)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-bert", action="store_true", help="skip the BERT-base ms/batch measurement")
     return ap.parse_args()
 
 
@@ -66,6 +77,64 @@ def algorithmic_bytes(seq, refetch_frac):
     scale, V and O (fp16), plus the LSB plane for the refetched share."""
     rows = B * H * seq
     return rows * (D + 4 + D // 2 + 4 + 2 * D + 2 * D) + refetch_frac * rows * (D // 2) + B * seq * 4
+
+
+def algorithmic_work(seq, refetch_frac):
+    """Per launch: int8 ops of the scores (MSB score for every row, full score
+    for the refetched rows), fp16 flops of P.V, and exp2 evaluations (MSB
+    statistics, full statistics of the refetched rows, the final P)."""
+    units = B * H * seq * seq
+    return {"int8_ops": 2 * units * D * (1 + refetch_frac),
+            "f16_flops": 2 * units * D,
+            "exp2": units * (2 + refetch_frac)}
+
+
+def measure_peaks(torch, dev):
+    """Measured denominators the peaks file lacks: MUFU exp2 rate (own
+    microbenchmark, lib/libspatten_peaks.so) and int8 tensor-core rate
+    (torch._int_mm, cuBLASLt) -- best of several timed launches each."""
+    import ctypes
+    out = {}
+    st = torch.cuda.current_stream(dev)
+
+    def best(fn, n=6):
+        t = []
+        for i in range(n + 2):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            fn()
+            b.record(st)
+            b.synchronize()
+            if i >= 2:
+                t.append(a.elapsed_time(b) * 1e-3)
+        return min(t)
+
+    try:
+        lib = ctypes.CDLL(os.path.join(ROOT, "spatten_b200", "lib", "libspatten_peaks.so"))
+        lib.spatten_peak_ex2.restype = ctypes.c_longlong
+        lib.spatten_peak_ex2.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        blocks = sms * 8
+        buf = torch.empty(blocks * 256, dtype=torch.float32, device=dev)
+        n = {}
+
+        def run():
+            n["ops"] = lib.spatten_peak_ex2(blocks, 4096, ctypes.c_void_p(buf.data_ptr()),
+                                            ctypes.c_void_p(st.cuda_stream))
+        sec = best(run)
+        out["exp2_per_s"] = n["ops"] / sec if n.get("ops") else None
+    except OSError:
+        out["exp2_per_s"] = None
+    try:
+        a = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device=dev)
+        b = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device=dev)
+        sec = best(lambda: torch._int_mm(a, b))
+        out["int8_ops_per_s"] = 2 * 8192 ** 3 / sec
+        del a, b
+    except (RuntimeError, AttributeError):
+        out["int8_ops_per_s"] = None
+    return out
 
 
 class ClockSampler:
@@ -140,6 +209,60 @@ def cpu_sample(torch, q, k, v, heads):
     return time.perf_counter() - t0
 
 
+BERT_CPU_KNOBS = dict(enable_head_prune=True, head_keep_ratio=0.9, enable_token_prune=True,
+                      token_keep_ratio=0.9, enable_v_prune=True, v_prune_threshold=1e-3)
+
+
+def bert_cpu_inputs(torch):
+    """BERT-base random init (seed 0, fp32) and ids [1, 128] from seed 0 --
+    the reference's CPU configuration."""
+    from transformers import BertConfig, BertModel
+    torch.manual_seed(0)
+    model = BertModel(BertConfig(attn_implementation="eager")).eval()
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(1000, 30522, (1, 128), generator=g)
+    return model, ids, torch.ones_like(ids)
+
+
+def reference_bert_cpu(torch, runs=10):
+    """The reference's cascade BERT forward (restated bit-exactly by
+    oracle.bert) on the host cores: median ms of `runs` after 3 warm-ups."""
+    from oracle.bert import LayerKnobs, spatten_bert_forward
+    model, ids, mask = bert_cpu_inputs(torch)
+    kn = LayerKnobs(**BERT_CPU_KNOBS)
+    ts = []
+    with torch.no_grad():
+        for i in range(runs + 3):
+            t0 = time.perf_counter()
+            spatten_bert_forward(model, ids, mask, kn)
+            if i >= 3:
+                ts.append(time.perf_counter() - t0)
+    ts.sort()
+    return ts[len(ts) // 2] * 1e3
+
+
+def ours_bert_b1(torch, dev, runs=10):
+    """The same B1 S128 fp32 forward through the patched model on the GPU."""
+    import copy
+    from spatten_b200.bert import patch_bert
+    model, ids, mask = bert_cpu_inputs(torch)
+    m = patch_bert(copy.deepcopy(model).to(dev).eval(), **BERT_CPU_KNOBS)
+    ids, mask = ids.to(dev), mask.to(dev)
+    st = torch.cuda.current_stream(dev)
+    with torch.no_grad():
+        for _ in range(3):
+            m(input_ids=ids, attention_mask=mask)
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(runs):
+            m(input_ids=ids, attention_mask=mask)
+        e1.record(st)
+        torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / runs
+
+
 def reference_arm(args, torch, rank, world):
     if rank != 0:
         return
@@ -170,7 +293,63 @@ def reference_arm(args, torch, rank, world):
                              "sample": f"one batch element (all {H} heads, S={seq}) per step, "
                                        "torch fp32 restatement of the op on the host cores"},
             "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not args.no_bert:
+        line["bert"] = {"ms_per_batch": reference_bert_cpu(torch), "batch": 1, "seq_len": 128,
+                        "dtype": "fp32", "cores": nthreads,
+                        "config": "BERT-base random init seed 0, ids seed 0, token/head keep 0.9, "
+                                  "V prune 1e-3: the reference's cascade on the host cores"}
     print(json.dumps(line), flush=True)
+
+
+BERT_B, BERT_S = 32, 512
+BERT_KNOBS = dict(enable_head_prune=True, head_keep_ratio=0.9, enable_token_prune=True,
+                  token_keep_ratio=0.9, enable_v_prune=True, v_prune_threshold=1e-3,
+                  enable_prog_quant=True, quant_threshold=0.1)
+
+
+def bert_bench(torch, rank, world, dev, steps=5):
+    """BERT-base SpAtten forward, fp16, random-init weights (seed 0), batch 32
+    of random token ids at seq 512, token/head keep 0.9, V prune 1e-3,
+    progressive quantisation 0.1; the batch is sharded over the ranks and the
+    head importance all-reduced (batch-global head decisions). ms per global
+    batch = max over ranks."""
+    import torch.distributed as dist
+    from transformers import BertConfig, BertModel
+    from spatten_b200.bert import patch_bert
+    torch.manual_seed(0)
+    model = BertModel(BertConfig(attn_implementation="eager")).half().to(dev).eval()
+    knobs = dict(BERT_KNOBS)
+    if world > 1:
+        knobs["process_group"] = dist.group.WORLD
+    model = patch_bert(model, **knobs)
+    per = BERT_B // world
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(1000, 30522, (BERT_B, BERT_S), generator=g)[rank * per:(rank + 1) * per].to(dev)
+    mask = torch.ones_like(ids)
+    st = torch.cuda.current_stream(dev)
+    with torch.no_grad():
+        for _ in range(2):
+            model(input_ids=ids, attention_mask=mask)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            out = model(input_ids=ids, attention_mask=mask).last_hidden_state
+        e1.record(st)
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"ms_per_batch": ms, "batch": BERT_B, "seq_len": BERT_S, "per_rank_batch": per,
+            "dtype": "fp16", "steps": steps, "kept_tokens_last_layer": int(out.shape[1]),
+            "config": "BERT-base (12x768, 12 heads, FFN 3072) random init seed 0, random ids, "
+                      "token/head keep 0.9, V prune 1e-3, progressive quant 0.1, batch sharded "
+                      "over ranks with head-importance all-reduce"}
 
 
 def ours_arm(args, torch, rank, world, local_rank):
@@ -212,6 +391,9 @@ def ours_arm(args, torch, rank, world, local_rank):
     refetch_frac = float(r.refetch.float().mean())
     del q8, qs, kp, r
 
+    peaks = measure_peaks(torch, dev) if rank == 0 else {}
+    torch.cuda.synchronize(dev)
+
     sampler = ClockSampler(visible_gpu_index(local_rank))
     sampler.start()
     time.sleep(0.5)
@@ -231,33 +413,67 @@ def ours_arm(args, torch, rank, world, local_rank):
     ms = t0.elapsed_time(t1) / args.steps
     attn_ms = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
 
-    # end to end through the public API: pinned host in, host out
+    # End to end through the public API: every step copies its inputs from
+    # pinned host memory and its results back to pinned host memory. Copies
+    # run on their own streams so that step i+1's upload and step i-1's
+    # download overlap step i's compute (two device input buffers).
     out_h = torch.empty((B, H, seq, D), dtype=torch.float16).pin_memory()
     tok_h = torch.empty((B, seq), dtype=torch.float32).pin_memory()
     head_h = torch.empty((H,), dtype=torch.float32).pin_memory()
+    up = torch.cuda.Stream(dev)
+    down = torch.cuda.Stream(dev)
+    dbuf = [[torch.empty_like(t, device=dev) for t in (qh, kh, vh)] for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]     # compute done with a buffer
+    loaded = [torch.cuda.Event() for _ in range(2)]   # upload into a buffer done
+    done = torch.cuda.Event()                         # last download done
+    keep = []
 
-    def e2e_step():
-        qd, kd, vd = (t.to(dev, non_blocking=True) for t in (qh, kh, vh))
-        res = sp.progressive_attention(qd, kd, vd, refetch_threshold=REFETCH_THR,
-                                       v_prune_threshold=V_THR, sm_scale=SM_SCALE,
-                                       return_importance=True)
-        out_h.copy_(res.out, non_blocking=True)
-        tok_h.copy_(res.token_importance, non_blocking=True)
-        head_h.copy_(res.head_abs_sum, non_blocking=True)
+    def e2e_steps(n):
+        for i in range(n):
+            j = i % 2
+            with torch.cuda.stream(up):
+                if i >= 2:
+                    up.wait_event(free[j])
+                for d, h in zip(dbuf[j], (qh, kh, vh)):
+                    d.copy_(h, non_blocking=True)
+                loaded[j].record(up)
+            st.wait_event(loaded[j])
+            res = sp.progressive_attention(*dbuf[j], refetch_threshold=REFETCH_THR,
+                                           v_prune_threshold=V_THR, sm_scale=SM_SCALE,
+                                           return_importance=True)
+            free[j].record(st)
+            down.wait_stream(st)
+            with torch.cuda.stream(down):
+                out_h.copy_(res.out, non_blocking=True)
+                tok_h.copy_(res.token_importance, non_blocking=True)
+                head_h.copy_(res.head_abs_sum, non_blocking=True)
+                for t in (res.out, res.token_importance, res.head_abs_sum):
+                    t.record_stream(down)
+            keep.append(res)
+            del keep[:-2]
+        done.record(down)
+        st.wait_event(done)
+        st.wait_stream(up)
 
-    for _ in range(2):
-        e2e_step()
+    e2e_steps(2)
     torch.cuda.synchronize(dev)
     barrier()
     a0 = torch.cuda.Event(enable_timing=True)
     a1 = torch.cuda.Event(enable_timing=True)
     a0.record(st)
-    for _ in range(args.steps):
-        e2e_step()
+    up.wait_stream(st)
+    e2e_steps(args.steps)
     a1.record(st)
     torch.cuda.synchronize(dev)
     barrier()
     e2e_ms = a0.elapsed_time(a1) / args.steps
+    keep.clear()
+
+    bert = None
+    if not args.no_bert:
+        bert = bert_bench(torch, rank, world, dev)
+        if rank == 0:
+            bert["b1_s128_fp32_ms"] = ours_bert_b1(torch, dev)
 
     if world > 1:
         t = torch.tensor([ms, attn_ms, e2e_ms], device=dev)
@@ -267,34 +483,56 @@ def ours_arm(args, torch, rank, world, local_rank):
         return
     tokens = B * seq * world
     alg = algorithmic_bytes(seq, refetch_frac)
+    work = algorithmic_work(seq, refetch_frac)
+    measured = {}
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    peak, peak_src = 6650.0, "fallback"
     if os.path.exists(peaks_path):
         with open(peaks_path) as f:
-            peak = float(json.load(f).get("hbm_gbs", peak))
-        peak_src = "measured"
-    achieved = alg / (attn_ms * 1e-3) / 1e9
+            measured = json.load(f)
+    hbm_peak = float(measured.get("hbm_gbs", 6650.0))
+    tc_peak = float(measured.get("bf16_tflops", 1590.0))
+    peak_src = "measured" if measured else "fallback"
+    sec = attn_ms * 1e-3
+    hbm_gbs = alg / sec / 1e9
+    tensor_tflops = (work["int8_ops"] + work["f16_flops"]) / sec / 1e12
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "prog_attn_traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
-            traffic = json.load(f).get("dram_bytes_per_launch")
+            tr = json.load(f)
+        if tr.get("seq_len") == seq:
+            traffic = tr.get("dram_bytes_per_launch")
+    # The time floor of the launch: the slowest of HBM bytes, tensor work
+    # (int8 and fp16 at their measured rates) and exp2 on the MUFU.
+    i8_rate = peaks.get("int8_ops_per_s") or 2 * tc_peak * 1e12
+    ex2_rate = peaks.get("exp2_per_s")
+    floors = {"hbm_ms": alg / (hbm_peak * 1e9) * 1e3,
+              "tensor_ms": (work["int8_ops"] / i8_rate + work["f16_flops"] / (tc_peak * 1e12)) * 1e3,
+              "mufu_ms": work["exp2"] / ex2_rate * 1e3 if ex2_rate else None}
+    limiter = max((k for k in floors if floors[k] is not None), key=lambda k: floors[k])
+    t_bound = floors[limiter]
     line = {
         "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "s8 scores / f32 softmax / f16 P.V", "data": "synthetic", "config": config(seq),
-        "hbm_gbs": achieved, "attn_ms": attn_ms, "refetch_fraction": refetch_frac,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic,
-                     "peak_source": peak_src, "algorithmic_bytes": alg,
-                     "note": "attention launch incl. importance reduce; kernel is exp/ALU bound"},
+        "hbm_gbs": hbm_gbs, "attn_ms": attn_ms, "refetch_fraction": refetch_frac,
+        "roofline": {"bound": "tensor", "achieved": tensor_tflops, "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": tensor_tflops / tc_peak, "traffic": traffic,
+                     "peak_source": f"{peak_src} (bf16 burst)",
+                     "work_per_launch": work, "algorithmic_bytes": alg,
+                     "hbm": {"achieved_gbs": hbm_gbs, "peak_gbs": hbm_peak, "frac": hbm_gbs / hbm_peak},
+                     "t_bound": dict(floors, limiter=limiter.replace("_ms", ""), bound_ms=t_bound,
+                                     frac=t_bound / attn_ms,
+                                     int8_ops_per_s=i8_rate, exp2_per_s=ex2_rate)},
         "clocks": clocks,
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": 3 * B * H * seq * D * 2,
                 "d2h_bytes_per_step": B * H * seq * D * 2 + B * seq * 4 + H * 4},
     }
+    if bert is not None:
+        line["bert"] = bert
     if world == 1 and not args.no_cpu_baseline:
         qc, kc, vc = (t.cpu() for t in (qh, kh, vh))
         hs = H

@@ -7,6 +7,9 @@ parallel), then the objects link into ``spatten_b200/lib/libspatten_b200.so``
 with the CUDA runtime linked statically, so the library depends on nothing
 but the driver. The build is skipped when the library is newer than every
 source and header.
+
+``peaks/peaks.cu`` (the MUFU throughput microbenchmark the benchmark uses as
+a roofline denominator) links separately into ``lib/libspatten_peaks.so``.
 """
 import argparse
 import glob
@@ -22,6 +25,8 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB_DIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIB_DIR, "libspatten_b200.so")
+PEAKS_SRC = os.path.join(PKG, "peaks", "peaks.cu")
+PEAKS_LIB = os.path.join(LIB_DIR, "libspatten_peaks.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
          "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]
@@ -50,7 +55,23 @@ def up_to_date():
     return all(os.path.getmtime(d) <= t for d in _deps())
 
 
+def build_peaks(force=False):
+    """The measurement library (single source, no dependency on the main one)."""
+    if not force and os.path.exists(PEAKS_LIB) and \
+            os.path.getmtime(PEAKS_LIB) >= max(os.path.getmtime(PEAKS_SRC), os.path.getmtime(__file__)):
+        return PEAKS_LIB
+    os.makedirs(LIB_DIR, exist_ok=True)
+    tmp = PEAKS_LIB + ".tmp"
+    cmd = [nvcc(), *ARCH, *FLAGS, "-shared", "-cudart", "static", "-o", tmp, PEAKS_SRC]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {PEAKS_SRC}:\n{r.stderr}")
+    os.replace(tmp, PEAKS_LIB)
+    return PEAKS_LIB
+
+
 def build(force=False, verbose=False, ptxas_verbose=False):
+    build_peaks(force)
     if not force and up_to_date():
         return LIB
     os.makedirs(BUILD, exist_ok=True)
