@@ -127,6 +127,11 @@ typedef struct spatten_prog_attn_args {
   uint8_t* refetch_out; /* optional QUANT [Z, H, M]: 1 where the row was refetched */
   int32_t* score_out;   /* optional QUANT [Z, H, M, N]: the exact integer score each row used,
                            q8.(16*msb) or, for a refetched row, q8.k8 (for verification) */
+  int v_prune_count; /* count V prune (the reference's v_prune_num, spatten_bert.py:100-113):
+                        in rows of more than v_prune_count keys, zero the v_prune_count
+                        smallest probabilities (ties to the smaller key index), no
+                        renormalisation; 0 disables, at most 8; QUANT and DENSE only.
+                        Applies together with v_thr. (ABI version 2) */
 } spatten_prog_attn_args;
 
 /* Bytes of workspace spatten_prog_attn needs for these arguments (0 if no

@@ -18,6 +18,10 @@ threshold knobs of the B200 build:
   (``fractions.Fraction`` of the ratio's decimal repr).
 * ``v_prune_threshold`` replaces the reference's per-row top count
   (spatten_bert.py:100-113) by ``p < thr -> 0`` (no renormalisation).
+  Without it the count rule applies: with ``tie_rule="torch"`` exactly the
+  reference's ``torch.topk``, with ``"smallest_index"`` (the device rule)
+  the ``v_prune_num`` smallest by (score, key index); on the quantised core
+  always the latter.
 * ``enable_prog_quant`` routes the attention core through
   ``oracle.prog_attn.prog_attn_quant`` with ``quant_threshold`` as the row
   max-probability refetch threshold.
@@ -75,7 +79,7 @@ def _heads_view(x, n, d):
     return x.view(bs, s, n, d).permute(0, 2, 1, 3)
 
 
-def _attention_core_quant(q, k, v, mask, sm_scale, refetch_thr, v_thr):
+def _attention_core_quant(q, k, v, mask, sm_scale, refetch_thr, v_thr, v_count=0):
     from . import quant as oq
     from .prog_attn import prog_attn_quant
     qn = q.detach().numpy()
@@ -84,7 +88,7 @@ def _attention_core_quant(q, k, v, mask, sm_scale, refetch_thr, v_thr):
     msb, lsb, sk = oq.quant_k_planes(kn)
     bias = None if mask is None else mask.detach().numpy().astype(np.float32)
     r = prog_attn_quant(q8, sq, msb, lsb, sk, v.detach().numpy(), sm_scale, refetch_thr,
-                        v_thr or 0.0, bias=bias)
+                        v_thr or 0.0, bias=bias, v_count=v_count)
     ctx = torch.from_numpy(r["out"]).to(q.dtype)
     tok = torch.from_numpy(r["tok"]).to(q.dtype)
     return ctx, tok, r
@@ -118,9 +122,11 @@ def self_attention(attn, hidden, mask, active_heads, cumulative, kn: LayerKnobs,
     v = _heads_view(F.linear(hidden, wv, bv), cur, d)
     info = {}
     v_thr = kn.v_prune_threshold if kn.enable_v_prune else None
+    v_count = kn.v_prune_num if (kn.enable_v_prune and v_thr is None and kn.v_prune_num > 0
+                                 and seq_len > kn.v_prune_num) else 0
     if kn.enable_prog_quant:
         ctx, tok, r = _attention_core_quant(q, k, v, mask, 1.0 / math.sqrt(d),
-                                            kn.quant_threshold, v_thr)
+                                            kn.quant_threshold, v_thr, v_count)
         info["refetch"] = r["refetch"]
     else:
         scores = torch.matmul(q, k.transpose(-1, -2))
@@ -134,11 +140,20 @@ def self_attention(attn, hidden, mask, active_heads, cumulative, kn: LayerKnobs,
             if v_thr is not None:
                 probs = torch.where(probs < v_thr, torch.zeros_like(probs), probs)
             elif kn.v_prune_num > 0 and probs.size(-1) > kn.v_prune_num:
-                keep_v = probs.size(-1) - kn.v_prune_num
-                _, idx = torch.topk(probs, k=keep_v, dim=-1)
-                m = torch.zeros_like(probs)
-                m.scatter_(-1, idx, 1)
-                probs = probs * m
+                if tie_rule == "torch":
+                    keep_v = probs.size(-1) - kn.v_prune_num
+                    _, idx = torch.topk(probs, k=keep_v, dim=-1)
+                    m = torch.zeros_like(probs)
+                    m.scatter_(-1, idx, 1)
+                    probs = probs * m
+                else:
+                    # the device rule: drop the v_prune_num smallest by
+                    # (score, key index)
+                    from .prog_attn import _count_prune
+                    sc = scores.detach().reshape(-1, scores.shape[-1]).numpy()
+                    pr = probs.detach().reshape(-1, probs.shape[-1]).numpy().astype(np.float64)
+                    pp, _ = _count_prune(pr, sc, kn.v_prune_num)
+                    probs = torch.from_numpy(pp.astype(np.float32)).reshape(probs.shape)
         ctx = torch.matmul(probs, v)
         tok = probs.sum(dim=(1, 2))
     head_imp = ctx.abs().mean(dim=(0, 2, 3))

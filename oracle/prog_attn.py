@@ -14,7 +14,8 @@ Three modes, each a restatement for one (batch, head) at a time:
     Softmax/pruning/importance then follow spatten_bert.py:
       softmax over keys                         spatten_bert.py:93
       local V prune (new rule: p < v_thr -> 0,  spatten_bert.py:100-113
-        no renormalisation; the reference keeps a per-row top count)
+        no renormalisation; and/or the reference's count rule: zero the
+        v_count smallest p of each row, ties to the smaller key index)
       context = P' V                            spatten_bert.py:116
       head importance = sum |context|           spatten_bert.py:120-121
       token importance = sum_{h,q} P'           spatten_bert.py:136
@@ -77,17 +78,44 @@ def int_scores(q8, k8):
     return r.astype(np.int64).astype(np.int32)
 
 
-def _finish(p, vv, v_thr):
+def _count_prune(p, s, v_count):
+    """The reference's count rule (spatten_bert.py:100-113): in every row of
+    more than ``v_count`` keys, zero the ``v_count`` smallest probabilities
+    (no renormalisation). The order is that of the fp32 scores ``s`` (p is
+    monotone in s within a row), ties to the smaller key index. Returns the
+    pruned p and the smallest relative gap between the v_count-th and the
+    next score over rows where both are finite and differ (how robust the
+    choice is to the rounding of another implementation's scores)."""
+    m, n = s.shape
+    if v_count <= 0 or n <= v_count:
+        return p, np.inf
+    pp = p.copy()
+    gap = np.inf
+    keys = np.arange(n)
+    for r in range(m):
+        order = np.lexsort((keys, s[r].astype(np.float64)))
+        pp[r, order[:v_count]] = 0.0
+        a, b = float(s[r, order[v_count - 1]]), float(s[r, order[v_count]])
+        if np.isfinite(a) and np.isfinite(b) and a != b:  # exact ties order by key anywhere
+            gap = min(gap, abs(b - a) / max(abs(a), abs(b), 1e-30))
+    return pp, gap
+
+
+def _finish(p, vv, v_thr, s=None, v_count=0):
     pp = np.where(p < v_thr, 0.0, p) if v_thr > 0 else p
+    cgap = np.inf
+    if v_count > 0:
+        pp, cgap = _count_prune(pp, s, v_count)
     out = pp @ vv.astype(np.float64)
-    return pp, out
+    return pp, out, cgap
 
 
 def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.0,
-                    bias=None, causal=False, return_scores=False, band=1e-4):
+                    bias=None, causal=False, return_scores=False, band=1e-4, v_count=0):
     """Integer progressive attention. Shapes: q8 [Z,H,M,D] int8, sq [Z,H,M],
     msb_p/lsb_p [Z,Hkv,N,D/2] uint8 (packed, see oracle.quant), sk [Z,Hkv,N],
-    v [Z,Hkv,N,D]. Returns a dict of float64 outputs and diagnostics."""
+    v [Z,Hkv,N,D]. ``v_count`` > 0 applies the reference's count V prune (on
+    top of ``v_thr``). Returns a dict of float64 outputs and diagnostics."""
     from .quant import unpack_nibbles
     q8 = np.asarray(q8, np.int8)
     Z, H, M, D = q8.shape
@@ -99,6 +127,7 @@ def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.
     head_abs = np.zeros((Z, H))
     amb = np.zeros((Z, N))
     pgap = np.inf
+    cgap = np.inf
     scores = {}
     excl = _causal_mask(M, N) if causal else None
     for z in range(Z):
@@ -127,7 +156,9 @@ def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.
                 gap = np.min(np.abs(p - v_thr)) / v_thr
                 pgap = min(pgap, gap)
                 amb[z] += (np.abs(p - v_thr) < band * v_thr).sum(axis=0)
-            pp, o = _finish(p, np.asarray(v[z, kh]), v_thr)
+            s_ord = np.where(excl, -np.inf, s) if excl is not None else s
+            pp, o, g = _finish(p, np.asarray(v[z, kh]), v_thr, s_ord, v_count)
+            cgap = min(cgap, g)
             out[z, h] = o
             refetch[z, h] = rf
             maxprob[z, h] = mp
@@ -137,13 +168,13 @@ def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.
                 scores[(z, h)] = (A, F)
     res = dict(out=out, refetch=refetch, maxprob_msb=maxprob, tok_per_head=tok_h,
                tok=tok_h.sum(axis=1), head_abs=head_abs, vprune_gap=pgap, vprune_amb=amb,
-               refetch_gap=np.min(np.abs(maxprob - refetch_thr)) / max(abs(refetch_thr), 1e-30))
+               vcount_gap=cgap, refetch_gap=np.min(np.abs(maxprob - refetch_thr)) / max(abs(refetch_thr), 1e-30))
     if return_scores:
         res["scores"] = scores
     return res
 
 
-def prog_attn_dense(q, k, v, sm_scale, v_thr=0.0, bias=None, causal=False, band=1e-4):
+def prog_attn_dense(q, k, v, sm_scale, v_thr=0.0, bias=None, causal=False, band=1e-4, v_count=0):
     """Float attention with V pruning and importance (progressive quant off).
     Scores: fp32(q) . fp32(k) * sm_scale + bias, evaluated in float64 then
     rounded to fp32."""
@@ -155,6 +186,7 @@ def prog_attn_dense(q, k, v, sm_scale, v_thr=0.0, bias=None, causal=False, band=
     head_abs = np.zeros((Z, H))
     amb = np.zeros((Z, N))
     pgap = np.inf
+    cgap = np.inf
     excl = _causal_mask(M, N) if causal else None
     for z in range(Z):
         for h in range(H):
@@ -168,12 +200,14 @@ def prog_attn_dense(q, k, v, sm_scale, v_thr=0.0, bias=None, causal=False, band=
             if v_thr > 0:
                 pgap = min(pgap, np.min(np.abs(p - v_thr)) / v_thr)
                 amb[z] += (np.abs(p - v_thr) < band * v_thr).sum(axis=0)
-            pp, o = _finish(p, np.asarray(v[z, kh]), v_thr)
+            s_ord = np.where(excl, -np.inf, s) if excl is not None else s
+            pp, o, g = _finish(p, np.asarray(v[z, kh]), v_thr, s_ord, v_count)
+            cgap = min(cgap, g)
             out[z, h] = o
             tok_h[z, h] = pp.sum(axis=0)
             head_abs[z, h] = np.abs(o).sum()
     return dict(out=out, tok_per_head=tok_h, tok=tok_h.sum(axis=1), head_abs=head_abs,
-                vprune_gap=pgap, vprune_amb=amb)
+                vprune_gap=pgap, vprune_amb=amb, vcount_gap=cgap)
 
 
 def prog_attn_compat(q, k_msb, k_lsb, v, threshold, sm_scale, bm=32, bn=32):

@@ -23,7 +23,9 @@ Knobs (per attention module): ``enable_head_prune``/``head_prune_num``,
 ``enable_prog_quant``/``quant_threshold`` as in the reference, plus the ratio
 and threshold knobs ``head_keep_ratio``, ``token_keep_ratio`` (keep
 ``max(1, ceil(ratio * current))``, overriding the count) and
-``v_prune_threshold`` (zero ``p < thr``; used instead of the count when set).
+``v_prune_threshold`` (zero ``p < thr``; used instead of the count when set;
+without it ``v_prune_num`` <= 8 zeroes that many smallest probabilities of
+every row, ties to the smaller key index).
 ``quant_threshold`` is the row max-probability below which a row's LSB plane
 is refetched (the reference used it as a tile logit bound).
 
@@ -151,17 +153,22 @@ class SpattenBertSelfAttention(BertSelfAttention):
         k = qkv4[:, :, 1].permute(0, 2, 1, 3)
         v = qkv4[:, :, 2].permute(0, 2, 1, 3)
         bias = _mask_bias(attention_mask, B, S)
-        v_thr = 0.0
+        v_thr, v_count = 0.0, 0
         if self.enable_v_prune:
             if self.v_prune_threshold is not None:
                 v_thr = float(self.v_prune_threshold)
             elif self.v_prune_num > 0 and S > self.v_prune_num:
-                raise NotImplementedError(
-                    "count-based V pruning (v_prune_num) is not implemented on the B200 path; "
-                    "set v_prune_threshold")
+                # the reference's rule (spatten_bert.py:100-113): zero the
+                # v_prune_num smallest probabilities of every row
+                v_count = int(self.v_prune_num)
+                if v_count > N.MAX_V_PRUNE_COUNT:
+                    raise NotImplementedError(
+                        f"v_prune_num={v_count}: the B200 path prunes at most "
+                        f"{N.MAX_V_PRUNE_COUNT} keys per row by count; use v_prune_threshold")
         full = torch.zeros(B, S, H, d, dtype=hidden_states.dtype, device=dev)
         cum = self.cumulative_token_score
-        common = dict(sm_scale=1.0 / math.sqrt(d), v_thr=v_thr, bias=bias, tok_in=cum,
+        common = dict(sm_scale=1.0 / math.sqrt(d), v_thr=v_thr, v_prune_count=v_count, bias=bias,
+                      tok_in=cum,
                       want_tok=True, want_head=True, out=full.permute(0, 2, 1, 3),
                       out_head_map=heads, out_head_slots=H)
         if self.enable_prog_quant:

@@ -76,7 +76,7 @@ int spatten::set_last_error(int code, const char* msg) {
 
 extern "C" {
 
-int spatten_abi_version(void) { return 1; }
+int spatten_abi_version(void) { return 2; }
 
 const char* spatten_last_error(void) { return g_err.c_str(); }
 
@@ -149,6 +149,12 @@ static int fill_params(const spatten_prog_attn_args* a, spatten::AttnParams& p) 
       a->v_sz < 0 || a->v_sh < 0 || a->v_sn < 0 || a->o_sz < 0 || a->o_sh < 0 || a->o_sm < 0)
     return fail(SPATTEN_ERR_INVALID, "prog_attn: negative stride");
   if (a->tok_in && !a->tok_out) return fail(SPATTEN_ERR_INVALID, "prog_attn: tok_in without tok_out");
+  if (a->v_prune_count < 0) return fail(SPATTEN_ERR_INVALID, "prog_attn: negative v_prune_count");
+  if (a->v_prune_count > spatten::kMaxVPruneCount)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: v_prune_count %d > %d", a->v_prune_count,
+                spatten::kMaxVPruneCount);
+  if (a->v_prune_count > 0 && a->mode == SPATTEN_MODE_COMPAT)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: COMPAT has no count V prune");
   p.mode = a->mode;
   p.dtype = a->dtype;
   p.Z = a->Z; p.H = a->H; p.Hkv = a->Hkv; p.M = a->M; p.N = a->N; p.D = a->D;
@@ -163,6 +169,8 @@ static int fill_params(const spatten_prog_attn_args* a, spatten::AttnParams& p) 
   p.sm_scale = a->sm_scale; p.refetch_thr = a->refetch_thr; p.v_thr = a->v_thr;
   p.tile_m = a->tile_m; p.tile_n = a->tile_n; p.tile_thr = a->tile_thr;
   p.causal = a->causal;
+  // the reference prunes only rows longer than the count (spatten_bert.py:100)
+  p.v_count = a->N > a->v_prune_count ? a->v_prune_count : 0;
   p.refetch_out = quant ? a->refetch_out : nullptr;
   p.score_out = quant ? a->score_out : nullptr;
   const int rows = spatten::attn_tile_rows(p);

@@ -28,6 +28,7 @@ struct AttnParams {
   int tile_m, tile_n;
   float tile_thr;
   int causal;
+  int v_count;          // count V prune: zero the v_count smallest p of each row (0: off)
   uint8_t* refetch_out;
   int32_t* score_out;
   // workspace (per-CTA partial sums, reduced by importance_reduce)
@@ -39,6 +40,9 @@ struct AttnParams {
 cudaError_t launch_quant(int dtype, bool planes, const void* x, int Z, int H, int M, int D,
                          int64_t sz, int64_t sh, int64_t sm, int8_t* q8, uint8_t* msb,
                          uint8_t* lsb, float* scale, cudaStream_t st, int n_sm);
+
+// Largest count of the count V prune (smallest probabilities kept per thread).
+constexpr int kMaxVPruneCount = 8;
 
 // Rows of queries per CTA of the attention kernel (granularity of partials).
 int attn_tile_rows(const AttnParams& p);

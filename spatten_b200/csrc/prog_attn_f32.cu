@@ -8,6 +8,8 @@
 // query rows in turn; lane j owns keys j, j+32, ...; the per-CTA column sums
 // of P' live in shared memory (N <= kMaxN) and are written as the CTA's
 // token-importance partial.
+#include <climits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -89,6 +91,60 @@ struct F32Attn {
     l = ll;
   }
 
+  // Count V prune: the row's v_count-th smallest (score, key) pair over its
+  // keys, ties to the smaller key (each lane keeps its kMaxVPruneCount
+  // smallest pairs, then v_count rounds of a warp arg-min over the lists).
+  SPATTEN_DEV void count_threshold(int row, float c2, bool full, float& kvs, int& kvn) const {
+    float cv[kMaxVPruneCount];
+    int cn[kMaxVPruneCount];
+#pragma unroll
+    for (int q = 0; q < kMaxVPruneCount; ++q) {
+      cv[q] = INFINITY;
+      cn[q] = INT_MAX;
+    }
+    for (int n = lane; n < p.N; n += 32) {
+      float x = biased(score(n, c2, full), row, n);
+      int xn = n;
+      if (!(x < cv[kMaxVPruneCount - 1])) continue;
+#pragma unroll
+      for (int q = 0; q < kMaxVPruneCount; ++q) {
+        if (x < cv[q] || (x == cv[q] && xn < cn[q])) {
+          const float tv = cv[q];
+          const int tn = cn[q];
+          cv[q] = x;
+          cn[q] = xn;
+          x = tv;
+          xn = tn;
+        }
+      }
+    }
+    int head = 0;
+    for (int t = 0; t < p.v_count; ++t) {
+      float hv = INFINITY;
+      int hn = INT_MAX;
+#pragma unroll
+      for (int q = 0; q < kMaxVPruneCount; ++q)
+        if (q == head) {
+          hv = cv[q];
+          hn = cn[q];
+        }
+      float bv = hv;
+      int bn = hn;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int on = __shfl_xor_sync(0xffffffffu, bn, o);
+        if (ov < bv || (ov == bv && on < bn)) {
+          bv = ov;
+          bn = on;
+        }
+      }
+      kvs = bv;
+      kvn = bn;
+      if (hv == bv && hn == bn) ++head;  // keys are unique: the owning lane pops
+    }
+  }
+
   SPATTEN_DEV void run() {
     for (int i = lane; i < p.N; i += 32) colsum[i] = 0.f;
     __syncwarp();
@@ -120,6 +176,9 @@ struct F32Attn {
         if (full) stats(row, c2, true, m, l);
         if (p.refetch_out && lane == 0) p.refetch_out[((int64_t)z * p.H + h) * p.M + row] = full;
       }
+      float kvs = -INFINITY;
+      int kvn = -1;
+      if (p.v_count > 0) count_threshold(row, c2, full, kvs, kvn);
       const float inv_l = (m == -INFINITY || l <= 0.f) ? 0.f : 1.f / l;
       const float mm = m == -INFINITY ? 0.f : m;
       float o[D / 32];
@@ -133,6 +192,7 @@ struct F32Attn {
           const float s = biased(score(n, c2, full), row, n);
           pr = exp2f(s - mm) * inv_l;
           if (pr < p.v_thr) pr = 0.f;
+          if (p.v_count > 0 && (s < kvs || (s == kvs && n <= kvn))) pr = 0.f;
           colsum[n] += pr;
         }
         pc[lane] = pr;

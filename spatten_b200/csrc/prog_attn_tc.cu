@@ -29,6 +29,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <climits>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
@@ -138,7 +140,7 @@ SPATTEN_DEV f2 fadd2(f2 a, f2 b) {
 SPATTEN_DEV float i2f_exact(uint32_t x) { return __uint_as_float(x + 0x4B400000u); }
 constexpr float kMagic = 12582912.0f;
 
-template <int MODE, typename T, int D>
+template <int MODE, typename T, int D, bool VC>
 struct Cta {
   using L = Layout<MODE, T, D>;
   const TcParams& P;
@@ -482,8 +484,8 @@ struct Cta {
 
 // Q row r -> Q' operand (first D bytes for QUANT, 2D bytes for DENSE), zeros
 // if invalid; the two softmax threads of a row load alternate halves.
-template <int MODE, typename T, int D>
-SPATTEN_DEV void Cta<MODE, T, D>::load_q_row(int r, bool valid, int hf) {
+template <int MODE, typename T, int D, bool VC>
+SPATTEN_DEV void Cta<MODE, T, D, VC>::load_q_row(int r, bool valid, int hf) {
   const int row = m0 + r;
   uint8_t* base = sm + L::oQ;
   const int sw = r & 7;
@@ -508,8 +510,8 @@ SPATTEN_DEV void Cta<MODE, T, D>::load_q_row(int r, bool valid, int hf) {
   }
 }
 
-template <int MODE, typename T, int D>
-SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
+template <int MODE, typename T, int D, bool VC>
+SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
   constexpr int HC = BN / 2;        // columns per softmax thread and tile
   const int tid = threadIdx.x;      // 0 .. kSoftThreads-1
   const int warp = tid >> 5, lane = tid & 31;
@@ -702,6 +704,44 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
                       ? p.score_out + ((int64_t)z * p.H + h) * p.M * (int64_t)p.N
                       : nullptr;
   f2 inv2 = pack_f2(0.f, 0.f), mn2 = pack_f2(0.f, 0.f);
+  // Count V prune (VC): this thread's kMaxVPruneCount smallest (score, key)
+  // pairs of the scores its row ends up using, ascending in (score, key); the
+  // row's v_count-th smallest pair (kvs, kvn) then marks the keys to drop.
+  constexpr int KC = VC ? kMaxVPruneCount : 1;
+  float cv[KC];
+  int cn[KC];
+  float kvs = -INFINITY;
+  int kvn = -1;
+  auto track_reset = [&]() {
+#pragma unroll
+    for (int q = 0; q < KC; ++q) {
+      cv[q] = INFINITY;
+      cn[q] = INT_MAX;
+    }
+  };
+  auto track = [&](int j) {
+    const int n0 = j * BN + c0;
+    const int lim = p.N - n0;  // keys past N are not part of the row
+#pragma unroll
+    for (int i = 0; i < HC; ++i) {
+      float x = s[i];
+      if (i < lim && x < cv[KC - 1]) {
+        int xn = n0 + i;
+#pragma unroll
+        for (int q = 0; q < KC; ++q) {
+          if (x < cv[q] || (x == cv[q] && xn < cn[q])) {
+            const float tv = cv[q];
+            const int tn = cn[q];
+            cv[q] = x;
+            cn[q] = xn;
+            x = tv;
+            xn = tn;
+          }
+        }
+      }
+    }
+  };
+  if (VC) track_reset();
   int pairs_read = 0;
   const int npairs = (nt + 1) / 2;
   // One loop over the passes keeps a single copy of the tile code:
@@ -715,6 +755,7 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
       // ---- decide the refetch, build Q'
       if (MODE == kQuant) {
         flag = alive && valid && __frcp_rn(l_run) < p.refetch_thr;
+        if (VC && flag) track_reset();  // a refetched row ends up using its full scores
         // Q' bytes [D, 2D): q8 for a refetched row, zeros otherwise (each
         // thread of the row copies half of the chunks)
         uint8_t* base = sm + L::oQ;
@@ -757,6 +798,33 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
       const float mneg = (m_run == -INFINITY) ? 0.f : -m_run;
       inv2 = pack_f2(inv_l, inv_l);
       mn2 = pack_f2(mneg, mneg);
+      if (VC) {
+        // merge the two halves' lists (in P buffer 0, unused until the first
+        // P tile) up to the row's v_count-th smallest (score, key)
+        float* mvs = reinterpret_cast<float*>(sm + L::oP);
+        int* mns = reinterpret_cast<int*>(sm + L::oP + 2 * BM * KC * 4);
+#pragma unroll
+        for (int q = 0; q < KC; ++q) {
+          mvs[(hf * BM + r) * KC + q] = cv[q];
+          mns[(hf * BM + r) * KC + q] = cn[q];
+        }
+        named_sync(1, kSoftThreads);
+        const float* va = mvs + r * KC;
+        const float* vb = mvs + (BM + r) * KC;
+        const int* na = mns + r * KC;
+        const int* nb = mns + (BM + r) * KC;
+        int ia = 0, ib = 0;
+        for (int q = 0; q < p.v_count; ++q) {
+          const float xa = ia < KC ? va[ia] : INFINITY, xb = ib < KC ? vb[ib] : INFINITY;
+          const int ya = ia < KC ? na[ia] : INT_MAX, yb = ib < KC ? nb[ib] : INT_MAX;
+          const bool ta = xa < xb || (xa == xb && ya < yb);
+          kvs = ta ? xa : xb;
+          kvn = ta ? ya : yb;
+          ia += ta ? 1 : 0;
+          ib += ta ? 0 : 1;
+        }
+        named_sync(1, kSoftThreads);  // lists read before P overwrites the buffer
+      }
     }
     for (int j = 0; j < nt; ++j) {
       scores(j, s, pass == 2 ? dump : nullptr);
@@ -765,6 +833,7 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
           float m = pass == 0 ? m_run : mf;
           float l = pass == 0 ? l_run : lf;
           stats(s, m, l);
+          if (VC && (pass == 0 || flag)) track(j);
           if (pass == 0) {
             m_run = m;
             l_run = l;
@@ -778,6 +847,13 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
       // ---- pass 2 tile
       const int pb = j % kNP;
       if (alive) {
+        uint32_t drop = 0;  // count V prune: keys at or below (kvs, kvn)
+        if (VC) {
+          const int n0 = j * BN + c0;
+#pragma unroll
+          for (int i = 0; i < HC; ++i)
+            drop |= (uint32_t)(s[i] < kvs || (s[i] == kvs && n0 + i <= kvn)) << i;
+        }
 #pragma unroll
         for (int i = 0; i < HC; i += 2) {
           float a0, a1;
@@ -787,6 +863,10 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
         if (vthr > 0.f) {
 #pragma unroll
           for (int i = 0; i < HC; ++i) s[i] = s[i] < vthr ? 0.f : s[i];
+        }
+        if (VC) {
+#pragma unroll
+          for (int i = 0; i < HC; ++i) s[i] = (drop >> i) & 1u ? 0.f : s[i];
         }
         // P -> shared memory: A operand of P.V (K-major) and, read as an
         // MN-major operand, of the column sums; 128B swizzle
@@ -865,14 +945,14 @@ SPATTEN_DEV void Cta<MODE, T, D>::softmax_role() {
   }
 }
 
-template <int MODE, typename T, int D>
-__global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
+template <int MODE, typename T, int D, bool VC>
+__global__ void __launch_bounds__(kThreads, (D == 64 && !VC) ? 2 : 1)
     prog_attn_tc_kernel(const __grid_constant__ TcParams P) {
   extern __shared__ uint8_t smem_raw[];
   using L = Layout<MODE, T, D>;
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  Cta<MODE, T, D> c(P, base);
+  Cta<MODE, T, D, VC> c(P, base);
   const int warp = threadIdx.x >> 5;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(base + L::oTmem);
   if (threadIdx.x == 0) c.init_barriers();
@@ -926,7 +1006,7 @@ cudaError_t make_map(CUtensorMap* m, CUtensorMapDataType dt, int esz, const void
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int MODE, typename T, int D>
+template <int MODE, typename T, int D, bool VC>
 cudaError_t launch_tc_t(const AttnParams& a, cudaStream_t st) {
   using L = Layout<MODE, T, D>;
   TcParams P;
@@ -951,7 +1031,7 @@ cudaError_t launch_tc_t(const AttnParams& a, cudaStream_t st) {
   e = make_map(&P.tm_v, vdt, 2, a.v, D, a.N, a.Hkv, a.Z, a.v_sn * 2, a.v_sh * 2, a.v_sz * 2, 64,
                CU_TENSOR_MAP_SWIZZLE_128B);
   if (e != cudaSuccess) return e;
-  auto kern = prog_attn_tc_kernel<MODE, T, D>;
+  auto kern = prog_attn_tc_kernel<MODE, T, D, VC>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)a.mtiles, (unsigned)a.H, (unsigned)a.Z);
@@ -961,8 +1041,8 @@ cudaError_t launch_tc_t(const AttnParams& a, cudaStream_t st) {
 
 template <int MODE, typename T>
 cudaError_t launch_tc_d(const AttnParams& a, cudaStream_t st) {
-  if (a.D == 64) return launch_tc_t<MODE, T, 64>(a, st);
-  if (a.D == 128) return launch_tc_t<MODE, T, 128>(a, st);
+  if (a.D == 64) return a.v_count > 0 ? launch_tc_t<MODE, T, 64, true>(a, st) : launch_tc_t<MODE, T, 64, false>(a, st);
+  if (a.D == 128) return a.v_count > 0 ? launch_tc_t<MODE, T, 128, true>(a, st) : launch_tc_t<MODE, T, 128, false>(a, st);
   return cudaErrorInvalidValue;
 }
 

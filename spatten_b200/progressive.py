@@ -118,10 +118,12 @@ def _bias_view(bias, Z, H, M, Nk, device):
 def prog_attn(q, k0, v, *, mode, k1=None, q_scale=None, k_scale=None, sm_scale=None,
               refetch_thr=0.1, v_thr=0.0, bias=None, causal=False, tile=(32, 32), tile_thr=0.0,
               tok_in=None, want_tok=False, want_head=False, want_refetch=False, want_scores=False,
-              out=None, out_head_map=None, out_head_slots=0):
+              out=None, out_head_map=None, out_head_slots=0, v_prune_count=0):
     """General progressive attention (see spatten_prog_attn_args in
     include/spatten_b200.h). ``q`` int8 for QUANT; ``k0``/``k1`` are the
-    MSB/LSB planes (QUANT), k (DENSE) or k_msb/k_lsb (COMPAT)."""
+    MSB/LSB planes (QUANT), k (DENSE) or k_msb/k_lsb (COMPAT).
+    ``v_prune_count`` (0..8) zeroes that many smallest probabilities of
+    every row longer than it (the reference's count V prune)."""
     _cuda(q, k0, k1, v, q_scale, k_scale, bias, tok_in, out)
     q4, k04, v4 = _as4d(q, "q"), _as4d(k0, "k"), _as4d(v, "v")
     k14 = None if k1 is None else _as4d(k1, "k1")
@@ -162,6 +164,7 @@ def prog_attn(q, k0, v, *, mode, k1=None, q_scale=None, k_scale=None, sm_scale=N
     a.sm_scale, a.refetch_thr, a.v_thr = float(sm_scale), float(refetch_thr), float(v_thr)
     a.tile_m, a.tile_n, a.tile_thr = int(tile[0]), int(tile[1]), float(tile_thr)
     a.causal = int(bool(causal))
+    a.v_prune_count = int(v_prune_count)
     tok = torch.empty((Z, Nk), dtype=torch.float32, device=v.device) if (want_tok or tok_in is not None) else None
     head = torch.empty((H,), dtype=torch.float32, device=v.device) if want_head else None
     ref = torch.empty((Z, H, M), dtype=torch.uint8, device=v.device) if want_refetch else None
@@ -201,16 +204,19 @@ def spatten_progressive_attention(q, k_msb, k_lsb, v, threshold=0.1):
 
 
 def progressive_attention(q, k, v, refetch_threshold=0.1, v_prune_threshold=0.0, sm_scale=None,
-                          attn_bias=None, causal=False, return_importance=False, k_planes=None):
+                          attn_bias=None, causal=False, return_importance=False, k_planes=None,
+                          v_prune_count=0):
     """Integer progressive attention on fp16/bf16 Q, K, V [Z, H, N, D].
 
     Returns ``out`` or, with ``return_importance``, an AttnResult with the
     token importance [Z, N], the per-head sum of |out| [H] and the refetch
-    flags [Z, H, M]. ``k_planes`` (a KPlanes) skips the quantisation of K."""
+    flags [Z, H, M]. ``k_planes`` (a KPlanes) skips the quantisation of K.
+    ``v_prune_count`` applies the reference's count V prune as well."""
     q8, qs = quant_q_int8(q)
     kp = k_planes if k_planes is not None else quant_k_planes(k)
     r = prog_attn(q8, kp.msb, v, k1=kp.lsb, mode=N.MODE_QUANT, q_scale=qs, k_scale=kp.scale,
                   sm_scale=sm_scale, refetch_thr=refetch_threshold, v_thr=v_prune_threshold,
                   bias=attn_bias, causal=causal, want_tok=return_importance,
-                  want_head=return_importance, want_refetch=return_importance)
+                  want_head=return_importance, want_refetch=return_importance,
+                  v_prune_count=v_prune_count)
     return r if return_importance else r.out

@@ -94,6 +94,15 @@ def test_prog_attn_requires_workspace():
     assert b"workspace" in N.lib.spatten_last_error()
 
 
+@pytest.mark.parametrize("count,mode,code", [(-1, 0, "ERR_INVALID"), (9, 0, "ERR_UNSUPPORTED"),
+                                             (9, 1, "ERR_UNSUPPORTED"), (2, 2, "ERR_UNSUPPORTED")])
+def test_count_v_prune_limits(count, mode, code):
+    """The count V prune takes 0..8 keys per row, QUANT and DENSE only."""
+    from spatten_b200 import _native as N
+    a = _args(N, v_prune_count=count, mode=mode, tile_m=32, tile_n=32)
+    assert N.lib.spatten_prog_attn(a, ctypes.c_void_p(0x1000), 1 << 20, None) == getattr(N, code)
+
+
 def test_fp32_limits():
     from spatten_b200 import _native as N
     a = _args(N, dtype=N.DTYPE_F32, mode=N.MODE_COMPAT, tile_m=32, tile_n=32)
