@@ -48,8 +48,12 @@ def allreduce_head_importance(head_abs_sum, count, group=None):
     ``head_abs_sum`` [H] fp32: this rank's sum of |context| per head;
     ``count``: this rank's number of summed elements per head (B_local*S*D).
     Returns the batch-global mean, identical on every rank."""
-    buf = torch.cat([head_abs_sum.double().reshape(-1),
-                     torch.tensor([float(count)], dtype=torch.float64, device=head_abs_sum.device)])
+    # built on the device (a host-made tensor would copy from pageable memory
+    # and stall the host once per layer)
+    n = head_abs_sum.numel()
+    buf = torch.empty(n + 1, dtype=torch.float64, device=head_abs_sum.device)
+    buf[:n].copy_(head_abs_sum.reshape(-1))
+    buf[n:].fill_(float(count))
     dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
     return (buf[:-1] / buf[-1]).to(torch.float32)
 
