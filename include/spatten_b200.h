@@ -132,6 +132,10 @@ typedef struct spatten_prog_attn_args {
                         smallest probabilities (ties to the smaller key index), no
                         renormalisation; 0 disables, at most 8; QUANT and DENSE only.
                         Applies together with v_thr. (ABI version 2) */
+  const int32_t* key_limit; /* optional [Z, M] int32, QUANT and DENSE: row m of batch z sees
+                               keys n < key_limit[z*M + m] only (the causal mask of a
+                               position-sorted subset of keys, e.g. a pruned KV cache);
+                               replaces `causal` when set. (ABI version 3) */
 } spatten_prog_attn_args;
 
 /* Bytes of workspace spatten_prog_attn needs for these arguments (0 if no

@@ -61,15 +61,22 @@ def _causal_mask(m, n):
     return j > i + (n - m)
 
 
+def _limit_mask(limit, n):
+    """Excluded keys of rows that see keys n < limit[m] only."""
+    return np.arange(n)[None, :] >= np.asarray(limit)[:, None]
+
+
 def _softmax_rows(s, excluded=None):
     """float64 softmax over the last axis; ``excluded`` entries get p = 0."""
     s64 = s.astype(np.float64)
     if excluded is not None:
         s64 = np.where(excluded, -np.inf, s64)
     mx = np.max(s64, axis=-1, keepdims=True)
-    e = np.exp(s64 - mx)
+    none = ~np.isfinite(mx)  # a row that sees no key: p = 0, l = 0
+    e = np.where(none, 0.0, np.exp(s64 - np.where(none, 0.0, mx)))
     l = np.sum(e, axis=-1, keepdims=True)
-    return e / l, mx[..., 0], l[..., 0]
+    p = np.where(l > 0, e / np.where(l > 0, l, 1.0), 0.0)
+    return p, mx[..., 0], l[..., 0]
 
 
 def int_scores(q8, k8):
@@ -111,11 +118,13 @@ def _finish(p, vv, v_thr, s=None, v_count=0):
 
 
 def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.0,
-                    bias=None, causal=False, return_scores=False, band=1e-4, v_count=0):
+                    bias=None, causal=False, return_scores=False, band=1e-4, v_count=0,
+                    key_limit=None):
     """Integer progressive attention. Shapes: q8 [Z,H,M,D] int8, sq [Z,H,M],
     msb_p/lsb_p [Z,Hkv,N,D/2] uint8 (packed, see oracle.quant), sk [Z,Hkv,N],
     v [Z,Hkv,N,D]. ``v_count`` > 0 applies the reference's count V prune (on
-    top of ``v_thr``). Returns a dict of float64 outputs and diagnostics."""
+    top of ``v_thr``). ``key_limit`` [Z, M]: row m sees keys n < key_limit[z, m]
+    (replaces ``causal``). Returns a dict of float64 outputs and diagnostics."""
     from .quant import unpack_nibbles
     q8 = np.asarray(q8, np.int8)
     Z, H, M, D = q8.shape
@@ -129,8 +138,9 @@ def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.
     pgap = np.inf
     cgap = np.inf
     scores = {}
-    excl = _causal_mask(M, N) if causal else None
+    excl0 = _causal_mask(M, N) if causal else None
     for z in range(Z):
+        excl = _limit_mask(key_limit[z], N) if key_limit is not None else excl0
         for h in range(H):
             kh = _kv_head(h, H, Hkv)
             msb = unpack_nibbles(msb_p[z, kh], signed=True).astype(np.int16)
@@ -174,7 +184,8 @@ def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.
     return res
 
 
-def prog_attn_dense(q, k, v, sm_scale, v_thr=0.0, bias=None, causal=False, band=1e-4, v_count=0):
+def prog_attn_dense(q, k, v, sm_scale, v_thr=0.0, bias=None, causal=False, band=1e-4, v_count=0,
+                    key_limit=None):
     """Float attention with V pruning and importance (progressive quant off).
     Scores: fp32(q) . fp32(k) * sm_scale + bias, evaluated in float64 then
     rounded to fp32."""
@@ -187,8 +198,9 @@ def prog_attn_dense(q, k, v, sm_scale, v_thr=0.0, bias=None, causal=False, band=
     amb = np.zeros((Z, N))
     pgap = np.inf
     cgap = np.inf
-    excl = _causal_mask(M, N) if causal else None
+    excl0 = _causal_mask(M, N) if causal else None
     for z in range(Z):
+        excl = _limit_mask(key_limit[z], N) if key_limit is not None else excl0
         for h in range(H):
             kh = _kv_head(h, H, Hkv)
             s = (q[z, h].astype(np.float64) @ np.asarray(k[z, kh], np.float64).T).astype(np.float32)

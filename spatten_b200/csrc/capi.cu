@@ -76,7 +76,7 @@ int spatten::set_last_error(int code, const char* msg) {
 
 extern "C" {
 
-int spatten_abi_version(void) { return 2; }
+int spatten_abi_version(void) { return 3; }
 
 const char* spatten_last_error(void) { return g_err.c_str(); }
 
@@ -155,6 +155,9 @@ static int fill_params(const spatten_prog_attn_args* a, spatten::AttnParams& p) 
                 spatten::kMaxVPruneCount);
   if (a->v_prune_count > 0 && a->mode == SPATTEN_MODE_COMPAT)
     return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: COMPAT has no count V prune");
+  if (a->key_limit && a->mode == SPATTEN_MODE_COMPAT)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: COMPAT has no key_limit");
+  if (a->key_limit && !aligned(a->key_limit, 4)) return fail(SPATTEN_ERR_INVALID, "prog_attn: key_limit not aligned");
   p.mode = a->mode;
   p.dtype = a->dtype;
   p.Z = a->Z; p.H = a->H; p.Hkv = a->Hkv; p.M = a->M; p.N = a->N; p.D = a->D;
@@ -171,6 +174,8 @@ static int fill_params(const spatten_prog_attn_args* a, spatten::AttnParams& p) 
   p.causal = a->causal;
   // the reference prunes only rows longer than the count (spatten_bert.py:100)
   p.v_count = a->N > a->v_prune_count ? a->v_prune_count : 0;
+  p.key_limit = a->key_limit;
+  if (a->key_limit) p.causal = 0;
   p.refetch_out = quant ? a->refetch_out : nullptr;
   p.score_out = quant ? a->score_out : nullptr;
   const int rows = spatten::attn_tile_rows(p);

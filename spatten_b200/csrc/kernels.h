@@ -29,6 +29,7 @@ struct AttnParams {
   float tile_thr;
   int causal;
   int v_count;          // count V prune: zero the v_count smallest p of each row (0: off)
+  const int32_t* key_limit;  // [Z, M]: row m sees keys n < key_limit[z*M+m] (null: causal / all)
   uint8_t* refetch_out;
   int32_t* score_out;
   // workspace (per-CTA partial sums, reduced by importance_reduce)

@@ -64,6 +64,7 @@ struct F32Attn {
     if (p.bias)
       s += p.bias[(int64_t)z * p.b_sz + (int64_t)h * p.b_sh + (int64_t)row * p.b_sm + (int64_t)n * p.b_sn] * kLog2e;
     if (p.causal && n > row + (p.N - p.M)) s = -INFINITY;
+    if (p.key_limit && n >= p.key_limit[(int64_t)z * p.M + row]) s = -INFINITY;
     return s;
   }
 

@@ -91,7 +91,7 @@ struct Layout {
   static constexpr int oBar = oHs + 4 * kSoftWarps;     // mbarriers
   static constexpr int kNumBars = 2 * kNStg + 2 * kNExp + 2 * 2 + 2 * kNP + 2 * kNV + 2 * 2 + 3;
   static constexpr int oTmem = oBar + kNumBars * 8;
-  static constexpr int oFlag = oTmem + 4;  // int abort, int decision
+  static constexpr int oFlag = oTmem + 4;  // int abort, int decision, int key tiles of the CTA
   static constexpr int kBytes = oFlag + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
@@ -177,6 +177,29 @@ struct Cta {
     kvh = h / (p.H / p.Hkv);
     m0 = mt * BM;
     nt = (p.N + BN - 1) / BN;
+  }
+
+  // Key tiles this CTA visits (warp 0, before the start barrier): with a
+  // causal mask or key_limit, tiles past the largest limit of the CTA's rows
+  // are masked for every row and are skipped. The count V prune visits them
+  // all (masked keys take part in its count), and so does the verification
+  // dump of the integer scores (it records every key's score).
+  SPATTEN_DEV void count_key_tiles() {
+    const int lane = threadIdx.x & 31;
+    int lim = p.N;
+    if (!VC && !p.score_out && (p.key_limit || p.causal)) {
+      int mx = 0;
+      const int rows = min(BM, p.M - m0);
+      for (int i = lane; i < rows; i += 32) {
+        const int row = m0 + i;
+        const int kl = p.key_limit ? p.key_limit[(int64_t)z * p.M + row] : row + (p.N - p.M) + 1;
+        mx = max(mx, kl);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      lim = min(p.N, max(mx, 1));
+    }
+    if (lane == 0) *reinterpret_cast<int*>(sm + L::oFlag + 8) = (lim + BN - 1) / BN;
   }
 
   SPATTEN_DEV void init_barriers() {
@@ -542,6 +565,9 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
   const float* brow = gen_bias ? p.bias + (int64_t)z * p.b_sz + (int64_t)h * p.b_sh + (int64_t)row * p.b_sm
                                : nullptr;
   const int shift = p.N - p.M;
+  // keys this row sees: n < klim (key_limit, causal diagonal, or all)
+  const int klim = p.key_limit ? (valid ? p.key_limit[(int64_t)z * p.M + row] : 0)
+                               : (p.causal ? row + shift + 1 : p.N);
   const float* ksm = reinterpret_cast<const float*>(sm + L::oKs);
   const float* kbm = reinterpret_cast<const float*>(sm + L::oKb);
   float* stm = reinterpret_cast<float*>(sm + L::oSt);  // [2][2][BM]
@@ -611,8 +637,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
     }
     // keys past N and, with the causal mask, keys after the row's diagonal:
     // only tiles that reach them pay for the per-element test
-    int lim = p.N - n0;
-    if (p.causal) lim = min(lim, row + shift + 1 - n0);
+    const int lim = min(p.N, klim) - n0;
     if (lim < HC) {
 #pragma unroll
       for (int i = 0; i < HC; ++i)
@@ -691,7 +716,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
     __syncwarp();
     if (lane == 0) mbar_arrive(&b.cs_empty[cb]);
     const int key = pi * 2 * BN + qd * 32 + lane;
-    if (key < p.N) tokp[key] = __uint_as_float(v);
+    if (key < p.N && key < nt * BN) tokp[key] = __uint_as_float(v);
   };
 
   float s[HC];
@@ -894,6 +919,8 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
   }
   if (want_tok && hf == 0)
     while (pairs_read < npairs) read_pair(pairs_read++);
+  if (want_tok)  // skipped key tiles: no probability reached them
+    for (int key = nt * BN + tid; key < p.N; key += kSoftThreads) tokp[key] = 0.f;
 
   // ---- epilogue: O (already normalised) from TMEM, this thread's half row
   if (!mbar_wait(b.o_full, 0, kErrSoftmax | 4, abort)) alive = false;
@@ -956,6 +983,7 @@ __global__ void __launch_bounds__(kThreads, (D == 64 && !VC) ? 2 : 1)
   const int warp = threadIdx.x >> 5;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(base + L::oTmem);
   if (threadIdx.x == 0) c.init_barriers();
+  if (warp == 0) c.count_key_tiles();
   if (warp == kWarpMma) {
     tmem_alloc(tslot, L::kTmemCols);
     tmem_relinquish();
@@ -964,6 +992,7 @@ __global__ void __launch_bounds__(kThreads, (D == 64 && !VC) ? 2 : 1)
   __syncthreads();
   tc_fence_after();
   c.tmem = *tslot;
+  c.nt = *reinterpret_cast<volatile int*>(base + L::oFlag + 8);
   if (warp < kSoftWarps) c.softmax_role();
   else if (warp == kWarpTma) c.tma_role();
   else if (warp == kWarpMma) c.mma_role();

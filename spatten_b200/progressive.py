@@ -118,12 +118,14 @@ def _bias_view(bias, Z, H, M, Nk, device):
 def prog_attn(q, k0, v, *, mode, k1=None, q_scale=None, k_scale=None, sm_scale=None,
               refetch_thr=0.1, v_thr=0.0, bias=None, causal=False, tile=(32, 32), tile_thr=0.0,
               tok_in=None, want_tok=False, want_head=False, want_refetch=False, want_scores=False,
-              out=None, out_head_map=None, out_head_slots=0, v_prune_count=0):
+              out=None, out_head_map=None, out_head_slots=0, v_prune_count=0, key_limit=None):
     """General progressive attention (see spatten_prog_attn_args in
     include/spatten_b200.h). ``q`` int8 for QUANT; ``k0``/``k1`` are the
     MSB/LSB planes (QUANT), k (DENSE) or k_msb/k_lsb (COMPAT).
     ``v_prune_count`` (0..8) zeroes that many smallest probabilities of
-    every row longer than it (the reference's count V prune)."""
+    every row longer than it (the reference's count V prune). ``key_limit``
+    [Z, M] int: row m of batch z sees keys n < key_limit[z, m] only (causal
+    attention over a position-sorted subset of keys); replaces ``causal``."""
     _cuda(q, k0, k1, v, q_scale, k_scale, bias, tok_in, out)
     q4, k04, v4 = _as4d(q, "q"), _as4d(k0, "k"), _as4d(v, "v")
     k14 = None if k1 is None else _as4d(k1, "k1")
@@ -165,6 +167,12 @@ def prog_attn(q, k0, v, *, mode, k1=None, q_scale=None, k_scale=None, sm_scale=N
     a.tile_m, a.tile_n, a.tile_thr = int(tile[0]), int(tile[1]), float(tile_thr)
     a.causal = int(bool(causal))
     a.v_prune_count = int(v_prune_count)
+    if key_limit is not None:
+        _cuda(key_limit)
+        if tuple(key_limit.shape) != (Z, M):
+            raise ValueError(f"key_limit: shape {tuple(key_limit.shape)} (need {(Z, M)})")
+        key_limit = key_limit.to(torch.int32).contiguous()
+        a.key_limit = key_limit.data_ptr()
     tok = torch.empty((Z, Nk), dtype=torch.float32, device=v.device) if (want_tok or tok_in is not None) else None
     head = torch.empty((H,), dtype=torch.float32, device=v.device) if want_head else None
     ref = torch.empty((Z, H, M), dtype=torch.uint8, device=v.device) if want_refetch else None
