@@ -24,7 +24,8 @@ API with pinned host buffers (uploads and downloads overlap the previous /
 next step's compute on their own streams); and the BERT-base SpAtten forward
 in ms per batch (fp16 B32 S512 sharded over the ranks, and fp32 B1 S128 --
 the reference's CPU configuration, which the reference arm times on the host
-cores).
+cores); at N=1 also the Qwen3-0.6B-architecture prefill (bf16, 4 x 8192,
+cascade pruning of the KV cache) in ms.
 """
 import argparse
 import json
@@ -57,6 +58,7 @@ def parse():
     ap.add_argument("--seq", type=int, default=S)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-bert", action="store_true", help="skip the BERT-base ms/batch measurement")
+    ap.add_argument("--no-qwen3", action="store_true", help="skip the Qwen3 prefill measurement")
     return ap.parse_args()
 
 
@@ -352,6 +354,52 @@ def bert_bench(torch, rank, world, dev, steps=5):
                       "over ranks with head-importance all-reduce"}
 
 
+QWEN3_B, QWEN3_S = 4, 8192
+QWEN3_KNOBS = dict(enable_token_prune=True, token_keep_ratio=0.8, enable_prog_quant=True,
+                   quant_threshold=0.1)
+
+
+def qwen3_bench(torch, dev, steps=3):
+    """Qwen3-0.6B-architecture prefill (28 layers, hidden 1024, 16 Q / 8 KV
+    heads, head_dim 128, QK-norm, RoPE theta 1e6), bf16, random-init weights
+    (seed 0), batch 4 x 8192 random token ids: cascade token pruning keeps 0.8
+    of the keys per layer in the KV cache, progressive quantisation 0.1.
+    ms per prefill (hidden states of every position, KV cache filled)."""
+    from transformers import DynamicCache, Qwen3Config, Qwen3Model
+    from spatten_b200.qwen3 import patch_qwen3
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072,
+                      num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8,
+                      head_dim=128, max_position_embeddings=40960, rope_theta=1e6,
+                      tie_word_embeddings=True, attn_implementation="eager")
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = Qwen3Model(cfg)
+    model = patch_qwen3(model.to(torch.bfloat16).eval(), **QWEN3_KNOBS)
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (QWEN3_B, QWEN3_S), generator=g).to(dev)
+    st = torch.cuda.current_stream(dev)
+    with torch.no_grad():
+        for _ in range(2):
+            model(input_ids=ids, past_key_values=DynamicCache(config=cfg), use_cache=True)
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            model(input_ids=ids, past_key_values=DynamicCache(config=cfg), use_cache=True)
+        e1.record(st)
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    kept = [layer.self_attn.kept_positions.shape[1] for layer in model.layers]
+    del model
+    torch.cuda.empty_cache()
+    return {"ms_per_prefill": ms, "tokens_per_s": QWEN3_B * QWEN3_S / (ms * 1e-3),
+            "batch": QWEN3_B, "seq_len": QWEN3_S, "dtype": "bf16", "steps": steps,
+            "kept_keys_first_last_layer": [kept[0], kept[-1]],
+            "config": "Qwen3-0.6B architecture random init seed 0, random ids, cascade token "
+                      "pruning keep 0.8 per layer on the KV cache, progressive quant 0.1"}
+
+
 def ours_arm(args, torch, rank, world, local_rank):
     import torch.distributed as dist
     import spatten_b200 as sp
@@ -533,6 +581,8 @@ def ours_arm(args, torch, rank, world, local_rank):
     }
     if bert is not None:
         line["bert"] = bert
+    if world == 1 and not args.no_qwen3:
+        line["qwen3_prefill"] = qwen3_bench(torch, dev)
     if world == 1 and not args.no_cpu_baseline:
         qc, kc, vc = (t.cpu() for t in (qh, kh, vh))
         hs = H

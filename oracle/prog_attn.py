@@ -158,7 +158,8 @@ def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.
                 s_msb = (s_msb + bb).astype(np.float32)
                 s_full = (s_full + bb).astype(np.float32)
             _, _, l1 = _softmax_rows(s_msb, excl)
-            mp = 1.0 / l1
+            with np.errstate(divide="ignore"):  # a row that sees no key: l = 0
+                mp = 1.0 / l1
             rf = mp < refetch_thr
             s = np.where(rf[:, None], s_full, s_msb)
             p, _, _ = _softmax_rows(s, excl)

@@ -10,8 +10,11 @@ PyTorch-facing API:
 * ``spatten_b200.select``      -- cascade top-k and stream-compaction gathers.
 * ``spatten_b200.bert``        -- ``SpattenBertSelfAttention``,
   ``spatten_encoder_forward``, ``slice_linear_weights``, ``patch_bert``.
+* ``spatten_b200.qwen3``       -- ``SpattenQwen3Attention``, ``patch_qwen3``:
+  Qwen3 prefill with cascade token pruning of the KV cache.
 * ``spatten_b200.distributed`` -- batch / head sharding over ranks and the
   importance all-reduce.
+* ``spatten_b200.torch_ops``   -- the same operators under ``torch.ops.spatten``.
 """
 from ._native import LIB_PATH, SpattenError  # noqa: F401  (loads the library)
 from .progressive import (  # noqa: F401

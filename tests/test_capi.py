@@ -141,3 +141,12 @@ def test_ops_refuse_cpu_tensors():
         sp.quant_q_int8(x)
     with pytest.raises(ValueError, match="no CPU path"):
         sp.topk_indices(torch.zeros(4), 2)
+
+
+def test_torch_ops_registered():
+    """The operators are reachable by name under torch.ops.spatten."""
+    import torch
+    import spatten_b200.torch_ops  # noqa: F401
+    for name in ("quant_q_int8", "quant_k_planes", "progressive_attention", "topk_select",
+                 "gather_rows"):
+        assert hasattr(torch.ops.spatten, name), name
