@@ -370,7 +370,7 @@ def qwen3_bench(torch, dev, steps=3):
     cfg = Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072,
                       num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8,
                       head_dim=128, max_position_embeddings=40960, rope_theta=1e6,
-                      tie_word_embeddings=True, attn_implementation="eager")
+                      tie_word_embeddings=True, attn_implementation="sdpa")
     torch.manual_seed(0)
     with torch.device(dev):
         model = Qwen3Model(cfg)
