@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-bert", action="store_true", help="skip the BERT-base ms/batch measurement")
     ap.add_argument("--no-qwen3", action="store_true", help="skip the Qwen3 prefill measurement")
+    ap.add_argument("--only-qwen3", action="store_true",
+                    help="run only the Qwen3 prefill (--steps timed prefills) and print its line")
     return ap.parse_args()
 
 
@@ -329,26 +331,53 @@ def bert_bench(torch, rank, world, dev, steps=5):
     ids = torch.randint(1000, 30522, (BERT_B, BERT_S), generator=g)[rank * per:(rank + 1) * per].to(dev)
     mask = torch.ones_like(ids)
     st = torch.cuda.current_stream(dev)
-    with torch.no_grad():
-        for _ in range(2):
-            model(input_ids=ids, attention_mask=mask)
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
+
+    def timed(fn):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(st)
         for _ in range(steps):
-            out = model(input_ids=ids, attention_mask=mask).last_hidden_state
+            fn()
         e1.record(st)
         torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1) / steps
+        return e0.elapsed_time(e1) / steps
+
+    with torch.no_grad():
+        for _ in range(2):
+            ref = model(input_ids=ids, attention_mask=mask).last_hidden_state
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        eager_ms = timed(lambda: model(input_ids=ids, attention_mask=mask))
+        # One rank: the whole cascade forward as one CUDA graph (the kept
+        # token and head counts follow from the ratios, so every shape is
+        # static; the kept indices stay on the device).
+        graph_ms = None
+        if world == 1:
+            try:
+                side = torch.cuda.Stream(dev)
+                side.wait_stream(st)
+                with torch.cuda.stream(side):
+                    model(input_ids=ids, attention_mask=mask)
+                st.wait_stream(side)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    out_g = model(input_ids=ids, attention_mask=mask).last_hidden_state
+                g.replay()
+                torch.cuda.synchronize(dev)
+                if torch.equal(out_g, ref):
+                    graph_ms = timed(g.replay)
+                del g
+            except RuntimeError:
+                graph_ms = None
+    ms = eager_ms if graph_ms is None else graph_ms
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    return {"ms_per_batch": ms, "batch": BERT_B, "seq_len": BERT_S, "per_rank_batch": per,
-            "dtype": "fp16", "steps": steps, "kept_tokens_last_layer": int(out.shape[1]),
+    return {"ms_per_batch": ms, "launch": "cuda_graph" if graph_ms is not None else "eager",
+            "eager_ms_per_batch": eager_ms, "batch": BERT_B, "seq_len": BERT_S, "per_rank_batch": per,
+            "dtype": "fp16", "steps": steps, "kept_tokens_last_layer": int(ref.shape[1]),
             "config": "BERT-base (12x768, 12 heads, FFN 3072) random init seed 0, random ids, "
                       "token/head keep 0.9, V prune 1e-3, progressive quant 0.1, batch sharded "
                       "over ranks with head-importance all-reduce"}
@@ -359,7 +388,7 @@ QWEN3_KNOBS = dict(enable_token_prune=True, token_keep_ratio=0.8, enable_prog_qu
                    quant_threshold=0.1)
 
 
-def qwen3_bench(torch, dev, steps=3):
+def qwen3_bench(torch, dev, steps=3, warmup=2):
     """Qwen3-0.6B-architecture prefill (28 layers, hidden 1024, 16 Q / 8 KV
     heads, head_dim 128, QK-norm, RoPE theta 1e6), bf16, random-init weights
     (seed 0), batch 4 x 8192 random token ids: cascade token pruning keeps 0.8
@@ -379,7 +408,7 @@ def qwen3_bench(torch, dev, steps=3):
     ids = torch.randint(0, cfg.vocab_size, (QWEN3_B, QWEN3_S), generator=g).to(dev)
     st = torch.cuda.current_stream(dev)
     with torch.no_grad():
-        for _ in range(2):
+        for _ in range(warmup):
             model(input_ids=ids, past_key_values=DynamicCache(config=cfg), use_cache=True)
         torch.cuda.synchronize(dev)
         e0 = torch.cuda.Event(enable_timing=True)
@@ -602,6 +631,14 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, torch, rank, world)
+        return
+    if args.only_qwen3:
+        if rank == 0:
+            dev = torch.device("cuda", local_rank)
+            torch.cuda.set_device(dev)
+            q = qwen3_bench(torch, dev, steps=args.steps, warmup=args.warmup)
+            print(json.dumps(dict(metric="qwen3_prefill_ms", value=q["ms_per_prefill"], unit="ms",
+                                  higher_is_better=False, n_gpus=1, **q)), flush=True)
         return
     if world > 1:
         import datetime
