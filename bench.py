@@ -24,7 +24,9 @@ API with pinned host buffers (uploads and downloads overlap the previous /
 next step's compute on their own streams); and the BERT-base SpAtten forward
 in ms per batch (fp16 B32 S512 sharded over the ranks, and fp32 B1 S128 --
 the reference's CPU configuration, which the reference arm times on the host
-cores); at N=1 also the Qwen3-0.6B-architecture prefill (bf16, 4 x 8192,
+cores); the Qwen3-8B decode attention over a 32768-token progressive-quant
+KV cache with top-2048 selection (KV heads split over the ranks) with its HBM
+roofline; and at N=1 the Qwen3-0.6B-architecture prefill (bf16, 4 x 8192,
 cascade pruning of the KV cache) in ms.
 """
 import argparse
@@ -59,6 +61,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-bert", action="store_true", help="skip the BERT-base ms/batch measurement")
     ap.add_argument("--no-qwen3", action="store_true", help="skip the Qwen3 prefill measurement")
+    ap.add_argument("--no-decode", action="store_true", help="skip the Qwen3 decode measurement")
+    ap.add_argument("--only-decode", action="store_true",
+                    help="run only the Qwen3 decode attention (--steps timed steps) and print its line")
     ap.add_argument("--only-qwen3", action="store_true",
                     help="run only the Qwen3 prefill (--steps timed prefills) and print its line")
     return ap.parse_args()
@@ -355,6 +360,7 @@ def bert_bench(torch, rank, world, dev, steps=5):
         # token and head counts follow from the ratios, so every shape is
         # static; the kept indices stay on the device).
         graph_ms = None
+        graph_error = None
         if world == 1:
             try:
                 side = torch.cuda.Stream(dev)
@@ -369,15 +375,19 @@ def bert_bench(torch, rank, world, dev, steps=5):
                 torch.cuda.synchronize(dev)
                 if torch.equal(out_g, ref):
                     graph_ms = timed(g.replay)
+                else:
+                    graph_error = "graph output differs from the eager forward"
                 del g
-            except RuntimeError:
+            except RuntimeError as err:
                 graph_ms = None
+                graph_error = str(err).splitlines()[0][:200]
     ms = eager_ms if graph_ms is None else graph_ms
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     return {"ms_per_batch": ms, "launch": "cuda_graph" if graph_ms is not None else "eager",
+            "graph_error": graph_error,
             "eager_ms_per_batch": eager_ms, "batch": BERT_B, "seq_len": BERT_S, "per_rank_batch": per,
             "dtype": "fp16", "steps": steps, "kept_tokens_last_layer": int(ref.shape[1]),
             "config": "BERT-base (12x768, 12 heads, FFN 3072) random init seed 0, random ids, "
@@ -429,6 +439,66 @@ def qwen3_bench(torch, dev, steps=3, warmup=2):
             "kept_keys_first_last_layer": [kept[0], kept[-1]],
             "config": "Qwen3-0.6B architecture random init seed 0, random ids, cascade token "
                       "pruning keep 0.8 per layer on the KV cache, progressive quant 0.1"}
+
+
+DEC_B, DEC_H, DEC_G, DEC_N, DEC_D, DEC_TOPK, DEC_LAYERS = 64, 32, 8, 32768, 128, 2048, 36
+
+
+def decode_bench(torch, rank, world, dev, steps=3):
+    """Qwen3-8B-architecture decode attention (32 Q heads, 8 KV heads,
+    head_dim 128, 36 layers), bf16, batch 64, a KV cache of 32768 tokens with
+    K / V drawn N(0,1) from seed 0, K as 4-bit MSB / LSB planes, top-k keeps
+    2048 tokens per step. The KV heads are split over the ranks; the token
+    importance is all-reduced before the top-k. One layer's cache (6.5 GB at
+    one rank) serves all 36 layers' calls: every layer does the same work on
+    the same amount of memory. ms per decode step (36 layers), tokens/s
+    (batch / step) and the HBM roofline of one layer."""
+    import torch.distributed as dist
+    from spatten_b200.decode import decode_attention, quant_kv_cache
+    G, H = DEC_G // world, DEC_H // world
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    k = torch.randn(DEC_B, G, DEC_N, DEC_D, generator=g, device=dev, dtype=torch.bfloat16)
+    cache = quant_kv_cache(k, torch.randn(DEC_B, G, DEC_N, DEC_D, generator=g, device=dev,
+                                          dtype=torch.bfloat16))
+    del k
+    qs = [torch.randn(DEC_B, H, DEC_D, generator=g, device=dev, dtype=torch.bfloat16)
+          for _ in range(DEC_LAYERS)]
+    grp = dist.group.WORLD if world > 1 else None
+    st = torch.cuda.current_stream(dev)
+
+    def step():
+        for q in qs:
+            decode_attention(q, cache, top_k=DEC_TOPK, process_group=grp)
+
+    step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # algorithmic bytes of one layer at one rank: the MSB plane and scale of
+    # every cached key; both planes, the scale and V of every kept key; q, out
+    per_layer = (DEC_B * G * DEC_N * (DEC_D // 2 + 4) + DEC_B * G * DEC_TOPK * (DEC_D + 2 * DEC_D + 4)
+                 + 2 * DEC_B * H * DEC_D * 2)
+    layer_ms = ms / DEC_LAYERS
+    del cache, qs
+    torch.cuda.empty_cache()
+    return {"ms_per_step": ms, "tokens_per_s": DEC_B / (ms * 1e-3), "layer_ms": layer_ms,
+            "hbm_gbs_per_gpu": per_layer / (layer_ms * 1e-3) / 1e9, "algorithmic_bytes_per_layer_gpu": per_layer,
+            "batch": DEC_B, "cache_len": DEC_N, "top_k": DEC_TOPK, "layers": DEC_LAYERS,
+            "kv_heads_per_gpu": G, "dtype": "bf16",
+            "config": "Qwen3-8B decode attention: 32 Q / 8 KV heads, head_dim 128, K/V N(0,1), K as "
+                      "4-bit planes, importance all-reduced over KV-head shards, top-2048 per step"}
 
 
 def ours_arm(args, torch, rank, world, local_rank):
@@ -548,6 +618,7 @@ def ours_arm(args, torch, rank, world, local_rank):
     e2e_ms = a0.elapsed_time(a1) / args.steps
     keep.clear()
 
+    dec = None if args.no_decode else decode_bench(torch, rank, world, dev)
     bert = None
     if not args.no_bert:
         bert = bert_bench(torch, rank, world, dev)
@@ -612,6 +683,11 @@ def ours_arm(args, torch, rank, world, local_rank):
     }
     if bert is not None:
         line["bert"] = bert
+    if dec is not None:
+        hbm = dec["hbm_gbs_per_gpu"]
+        dec["roofline"] = {"bound": "hbm", "achieved": hbm, "peak": hbm_peak, "unit": "GB/s",
+                           "frac": hbm / hbm_peak}
+        line["qwen3_decode"] = dec
     if world == 1 and not args.no_qwen3:
         line["qwen3_prefill"] = qwen3_bench(torch, dev)
     if world == 1 and not args.no_cpu_baseline:
@@ -633,6 +709,25 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, torch, rank, world)
+        return
+    if args.only_decode:
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local_rank))
+        try:
+            dev = torch.device("cuda", local_rank)
+            torch.cuda.set_device(dev)
+            d = decode_bench(torch, rank, world, dev, steps=args.steps)
+            if rank == 0:
+                print(json.dumps(dict(metric="qwen3_decode_tokens_per_s", value=d["tokens_per_s"],
+                                      unit="tokens/s", higher_is_better=True, n_gpus=world, **d)), flush=True)
+        finally:
+            if world > 1:
+                import torch.distributed as dist
+                dist.destroy_process_group()
         return
     if args.only_qwen3:
         if rank == 0:

@@ -165,6 +165,50 @@ size_t spatten_prog_attn_noalloc_capacity(void);
 int spatten_prog_attn_noalloc(const spatten_prog_attn_args* a, void* stream);
 
 /*
+ * Decode attention over a progressive-quantised KV cache with top-k token
+ * selection: one new query per sequence, GQA (H query heads share G KV heads,
+ * H / G in {1, 2, 4, 8}), D in {64, 128}. The cache is the prefill format: K
+ * as packed 4-bit MSB / LSB planes [B, G, N, D/2] uint8 (byte p = dim p |
+ * dim p+D/2 << 4) with a per-key fp32 scale [B, G, N], V [B, G, N, D]
+ * fp16/bf16; keys 0 .. n_valid-1 hold data. Per step:
+ *   spatten_decode_importance: MSB scores q8 . 16*msb of every valid key
+ *     (only the MSB plane of the cache is read), softmax of every head over
+ *     the keys, importance[b, n] = sum over the H heads of those
+ *     probabilities (0 for n >= n_valid). With the KV heads split over ranks
+ *     each rank sums its own heads; all-reduce before the top-k.
+ *   spatten_topk_indices(importance, B, N, N, top_k, kept): the kept keys.
+ *   spatten_decode_attend: exact int8 scores q8 . k8 over the kept keys
+ *     (their LSB planes only), softmax, P.V -> out [B, H, D].
+ * This is SpAtten's cascade token pruning applied to decoding: the token
+ * importance of spatten_bert.py:136-150 over the cache, its top-k kept
+ * (spatten_bert.py:143-148), and progressive quantisation's LSB fetched for
+ * the kept keys only (spatten_bert_ultimate.py:58-74).
+ */
+typedef struct {
+  int dtype;              /* SPATTEN_DTYPE_F16 or _BF16: v and out */
+  int B, H, G, N, D;      /* batch, query heads, KV heads, cache length, head dim */
+  int n_valid;            /* 1 <= n_valid <= N */
+  const int8_t* q8;       /* [B, H, D] contiguous (spatten_quant_q_int8 of the query) */
+  const float* q_scale;   /* [B, H] */
+  const uint8_t* k_msb;   /* [B, G, N, D/2] contiguous */
+  const uint8_t* k_lsb;   /* [B, G, N, D/2] contiguous (attend) */
+  const float* k_scale;   /* [B, G, N] */
+  const void* v;          /* [B, G, N, D] contiguous (attend) */
+  float sm_scale;
+  float* importance;      /* [B, N] fp32 out (importance) */
+  int top_k;              /* kept keys per sequence (attend; sizes the workspace) */
+  const int64_t* kept;    /* [B, top_k] key indices (attend; out-of-range entries are skipped) */
+  void* out;              /* [B, H, D] out, dtype (attend) */
+} spatten_decode_args;
+
+/* Bytes of workspace both decode calls need (256-byte aligned). */
+size_t spatten_decode_workspace_size(const spatten_decode_args* a);
+int spatten_decode_importance(const spatten_decode_args* a, void* workspace, size_t workspace_bytes,
+                              void* stream);
+int spatten_decode_attend(const spatten_decode_args* a, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/*
  * Top-k selection, indices returned in ascending order:
  *   out[r, :] = sort(topk(x[r, :n], k).indices), r < rows
  * Ties at the k-th value go to the smaller index. x fp32 with row stride

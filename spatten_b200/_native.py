@@ -46,6 +46,17 @@ class ProgAttnArgs(ctypes.Structure):
     ]
 
 
+class DecodeArgs(ctypes.Structure):
+    """Mirror of spatten_decode_args (include/spatten_b200.h)."""
+    _fields_ = [
+        ("dtype", c_int), ("B", c_int), ("H", c_int), ("G", c_int), ("N", c_int), ("D", c_int),
+        ("n_valid", c_int),
+        ("q8", c_vp), ("q_scale", c_vp), ("k_msb", c_vp), ("k_lsb", c_vp), ("k_scale", c_vp),
+        ("v", c_vp), ("sm_scale", c_float), ("importance", c_vp), ("top_k", c_int), ("kept", c_vp),
+        ("out", c_vp),
+    ]
+
+
 # name -> (restype, argtypes); every entry point declared in include/spatten_b200.h
 SIGNATURES = {
     "spatten_abi_version": (c_int, []),
@@ -60,6 +71,9 @@ SIGNATURES = {
     "spatten_prog_attn_noalloc_capacity": (ctypes.c_size_t, []),
     "spatten_prog_attn_noalloc": (c_int, [ctypes.POINTER(ProgAttnArgs), c_vp]),
     "spatten_topk_indices": (c_int, [c_vp, c_int, c_int, c_i64, c_int, c_vp, c_vp]),
+    "spatten_decode_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(DecodeArgs)]),
+    "spatten_decode_importance": (c_int, [ctypes.POINTER(DecodeArgs), c_vp, ctypes.c_size_t, c_vp]),
+    "spatten_decode_attend": (c_int, [ctypes.POINTER(DecodeArgs), c_vp, ctypes.c_size_t, c_vp]),
     "spatten_gather_rows": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_int, c_int, c_int,
                                     c_i64, c_i64, c_vp, c_i64, c_i64, c_vp]),
 }

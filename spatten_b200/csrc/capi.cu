@@ -10,6 +10,7 @@
 
 #include "../../include/spatten_b200.h"
 #include "common.cuh"
+#include "decode.h"
 #include "kernels.h"
 
 namespace {
@@ -251,6 +252,96 @@ int spatten_gather_rows(const void* src, int64_t src_b_stride, int64_t src_r_str
                                             dst_b_stride, dst_r_stride, (cudaStream_t)stream,
                                             sm_count(), src_rows),
                      "gather launch");
+}
+
+// mode 0: sizing (shape and input checks only), 1: importance, 2: attend
+static int fill_decode(const spatten_decode_args* a, spatten::DecodeParams& p, int mode) {
+  const bool attend = mode == 2;
+  if (!a) return fail(SPATTEN_ERR_INVALID, "decode: null args");
+  if (a->dtype != SPATTEN_DTYPE_F16 && a->dtype != SPATTEN_DTYPE_BF16)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "decode: dtype %d (need f16 or bf16)", a->dtype);
+  if (a->B < 1 || a->H < 1 || a->G < 1 || a->N < 1)
+    return fail(SPATTEN_ERR_INVALID, "decode: empty shape B=%d H=%d G=%d N=%d", a->B, a->H, a->G, a->N);
+  if (a->H % a->G) return fail(SPATTEN_ERR_INVALID, "decode: H %% G != 0");
+  const int r = a->H / a->G;
+  if (r != 1 && r != 2 && r != 4 && r != 8)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "decode: %d query heads per KV head (need 1, 2, 4 or 8)", r);
+  if (a->D != 64 && a->D != 128) return fail(SPATTEN_ERR_UNSUPPORTED, "decode: D=%d (need 64 or 128)", a->D);
+  if (a->n_valid < 1 || a->n_valid > a->N)
+    return fail(SPATTEN_ERR_INVALID, "decode: n_valid %d outside [1, N=%d]", a->n_valid, a->N);
+  if (a->B > 65535 || a->G > 65535) return fail(SPATTEN_ERR_UNSUPPORTED, "decode: B or G > 65535");
+  if (!a->q8 || !a->q_scale || !a->k_msb || !a->k_scale)
+    return fail(SPATTEN_ERR_INVALID, "decode: null q8/q_scale/k_msb/k_scale");
+  if (!aligned(a->q8, 16) || !aligned(a->k_msb, 16) || !aligned(a->q_scale, 4) || !aligned(a->k_scale, 4))
+    return fail(SPATTEN_ERR_INVALID, "decode: q8/k_msb not 16-byte or scales not 4-byte aligned");
+  if (attend) {
+    if (!a->k_lsb || !a->v || !a->kept || !a->out)
+      return fail(SPATTEN_ERR_INVALID, "decode attend: null k_lsb/v/kept/out");
+    if (!aligned(a->k_lsb, 16) || !aligned(a->v, 16) || !aligned(a->out, 4) || !aligned(a->kept, 8))
+      return fail(SPATTEN_ERR_INVALID, "decode attend: k_lsb/v not 16-byte, out/kept not aligned");
+    if (a->top_k < 1) return fail(SPATTEN_ERR_INVALID, "decode attend: top_k %d < 1", a->top_k);
+  } else if (mode == 1) {
+    if (!a->importance) return fail(SPATTEN_ERR_INVALID, "decode importance: null importance");
+    if (!aligned(a->importance, 4)) return fail(SPATTEN_ERR_INVALID, "decode importance: not aligned");
+  }
+  p.dtype = a->dtype;
+  p.B = a->B; p.H = a->H; p.G = a->G; p.N = a->N; p.D = a->D; p.n_valid = a->n_valid;
+  p.q8 = a->q8; p.q_scale = a->q_scale; p.k_msb = a->k_msb; p.k_lsb = a->k_lsb;
+  p.k_scale = a->k_scale; p.v = a->v; p.sm_scale = a->sm_scale; p.importance = a->importance;
+  p.top_k = attend ? a->top_k : 1; p.kept = a->kept; p.out = a->out;
+  return SPATTEN_OK;
+}
+
+static void decode_layout(const spatten::DecodeParams& p, size_t (&off)[5]) {
+  const spatten::DecodeWorkspaceSizes s = spatten::decode_workspace_sizes(p);
+  off[0] = 0;
+  off[1] = off[0] + align256(s.scores);
+  off[2] = off[1] + align256(s.part);
+  off[3] = off[2] + align256(s.ml);
+  off[4] = off[3] + align256(s.o);
+}
+
+size_t spatten_decode_workspace_size(const spatten_decode_args* a) {
+  spatten::DecodeParams p;
+  if (fill_decode(a, p, 0) != SPATTEN_OK) return 0;
+  p.top_k = a->top_k > 0 ? a->top_k : 1;
+  size_t off[5];
+  decode_layout(p, off);
+  return off[4];
+}
+
+static int decode_workspace(const spatten::DecodeParams& p, void* ws, size_t bytes,
+                            spatten::DecodeWorkspace& w) {
+  size_t off[5];
+  decode_layout(p, off);
+  if (!ws || bytes < off[4])
+    return fail(SPATTEN_ERR_INVALID, "decode: workspace of %zu bytes needed, %zu given", off[4], bytes);
+  if (!aligned(ws, 256)) return fail(SPATTEN_ERR_INVALID, "decode: workspace not 256-byte aligned");
+  uint8_t* b = static_cast<uint8_t*>(ws);
+  w.scores = reinterpret_cast<float*>(b + off[0]);
+  w.part = reinterpret_cast<float*>(b + off[1]);
+  w.ml = reinterpret_cast<float*>(b + off[2]);
+  w.o = reinterpret_cast<float*>(b + off[3]);
+  return SPATTEN_OK;
+}
+
+int spatten_decode_importance(const spatten_decode_args* a, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  spatten::DecodeParams p;
+  if (int e = fill_decode(a, p, 1)) return e;
+  p.top_k = a->top_k > 0 ? a->top_k : 1;
+  spatten::DecodeWorkspace w;
+  if (int e = decode_workspace(p, workspace, workspace_bytes, w)) return e;
+  return cuda_status(spatten::launch_decode_importance(p, w, (cudaStream_t)stream), "decode importance launch");
+}
+
+int spatten_decode_attend(const spatten_decode_args* a, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  spatten::DecodeParams p;
+  if (int e = fill_decode(a, p, 2)) return e;
+  spatten::DecodeWorkspace w;
+  if (int e = decode_workspace(p, workspace, workspace_bytes, w)) return e;
+  return cuda_status(spatten::launch_decode_attend(p, w, (cudaStream_t)stream), "decode attend launch");
 }
 
 }  // extern "C"

@@ -150,3 +150,22 @@ def test_torch_ops_registered():
     for name in ("quant_q_int8", "quant_k_planes", "progressive_attention", "topk_select",
                  "gather_rows"):
         assert hasattr(torch.ops.spatten, name), name
+
+
+def test_decode_args_validation():
+    """The decode entry points validate before any launch; the workspace size
+    does not depend on which call follows."""
+    import ctypes
+    from spatten_b200 import _native as N
+    a = N.DecodeArgs()
+    a.dtype, a.B, a.H, a.G, a.N, a.D, a.n_valid = N.DTYPE_BF16, 2, 8, 2, 1000, 128, 900
+    a.q8 = a.q_scale = a.k_msb = a.k_lsb = a.k_scale = a.v = 1 << 20
+    a.sm_scale, a.top_k = 0.088, 100
+    n = N.lib.spatten_decode_workspace_size(a)
+    assert n > 0 and n % 256 == 0
+    assert N.lib.spatten_decode_importance(a, ctypes.c_void_p(1 << 24), n, None) == N.ERR_INVALID  # no output
+    a.H = 12  # 6 query heads per KV head
+    assert N.lib.spatten_decode_workspace_size(a) == 0
+    assert N.lib.spatten_decode_importance(a, None, 0, None) == N.ERR_UNSUPPORTED
+    a.H, a.n_valid = 8, 1001
+    assert N.lib.spatten_decode_attend(a, None, 0, None) == N.ERR_INVALID
