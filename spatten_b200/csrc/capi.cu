@@ -292,36 +292,38 @@ static int fill_decode(const spatten_decode_args* a, spatten::DecodeParams& p, i
   return SPATTEN_OK;
 }
 
-static void decode_layout(const spatten::DecodeParams& p, size_t (&off)[5]) {
+static void decode_layout(const spatten::DecodeParams& p, size_t (&off)[6]) {
   const spatten::DecodeWorkspaceSizes s = spatten::decode_workspace_sizes(p);
   off[0] = 0;
   off[1] = off[0] + align256(s.scores);
   off[2] = off[1] + align256(s.part);
-  off[3] = off[2] + align256(s.ml);
-  off[4] = off[3] + align256(s.o);
+  off[3] = off[2] + align256(s.st);
+  off[4] = off[3] + align256(s.ml);
+  off[5] = off[4] + align256(s.o);
 }
 
 size_t spatten_decode_workspace_size(const spatten_decode_args* a) {
   spatten::DecodeParams p;
   if (fill_decode(a, p, 0) != SPATTEN_OK) return 0;
   p.top_k = a->top_k > 0 ? a->top_k : 1;
-  size_t off[5];
+  size_t off[6];
   decode_layout(p, off);
-  return off[4];
+  return off[5];
 }
 
 static int decode_workspace(const spatten::DecodeParams& p, void* ws, size_t bytes,
                             spatten::DecodeWorkspace& w) {
-  size_t off[5];
+  size_t off[6];
   decode_layout(p, off);
-  if (!ws || bytes < off[4])
-    return fail(SPATTEN_ERR_INVALID, "decode: workspace of %zu bytes needed, %zu given", off[4], bytes);
+  if (!ws || bytes < off[5])
+    return fail(SPATTEN_ERR_INVALID, "decode: workspace of %zu bytes needed, %zu given", off[5], bytes);
   if (!aligned(ws, 256)) return fail(SPATTEN_ERR_INVALID, "decode: workspace not 256-byte aligned");
   uint8_t* b = static_cast<uint8_t*>(ws);
   w.scores = reinterpret_cast<float*>(b + off[0]);
   w.part = reinterpret_cast<float*>(b + off[1]);
-  w.ml = reinterpret_cast<float*>(b + off[2]);
-  w.o = reinterpret_cast<float*>(b + off[3]);
+  w.st = reinterpret_cast<float*>(b + off[2]);
+  w.ml = reinterpret_cast<float*>(b + off[3]);
+  w.o = reinterpret_cast<float*>(b + off[4]);
   return SPATTEN_OK;
 }
 

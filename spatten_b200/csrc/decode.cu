@@ -43,138 +43,188 @@ SPATTEN_DEV float2 load2<__nv_bfloat16>(const __nv_bfloat16* p) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
 }
 
-// Fused scores of one key for R heads: `w` holds the key's packed MSB plane
-// (D/2 bytes as D/8 words; byte p = dim p | dim p+D/2 << 4). With `lsb`, the
-// full int8 key k8 = 16*msb + lsb. q8 words of head r at qs[r*D/4 + ...].
-template <int D, int R>
-SPATTEN_DEV void key_dots(const uint32_t (&w)[D / 8], const uint32_t* lw, const uint32_t* qs,
-                          int (&acc)[R]) {
+// Exact int scores of K keys for R heads. w[k] holds key k's packed plane
+// words (D/8 words of the MSB plane; byte p = dim p | dim p+D/2 << 4); with
+// `lw` the LSB plane's, for the full int8 key k8 = 16*msb + lsb. The query
+// words of head r sit at qs[r*D/4 ..] in shared memory, read 16 bytes at a
+// time and shared by the K keys.
+template <int D, int R, int K>
+SPATTEN_DEV void key_dots(const uint32_t (&w)[K][D / 8], const uint32_t (*lw)[D / 8], const uint32_t* qs,
+                          int (&acc)[K][R]) {
+  const uint4* q4 = reinterpret_cast<const uint4*>(qs);
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    int a = 0;
-    const uint32_t* q = qs + r * (D / 4);
 #pragma unroll
-    for (int i = 0; i < D / 8; ++i) {
-      uint32_t lo = (w[i] << 4) & 0xF0F0F0F0u;  // 16*msb of dims 4i..4i+3
-      uint32_t hi = w[i] & 0xF0F0F0F0u;         // 16*msb of dims D/2+4i..
-      if (lw) {
-        lo |= lw[i] & 0x0F0F0F0Fu;
-        hi |= (lw[i] >> 4) & 0x0F0F0F0Fu;
+    for (int k = 0; k < K; ++k) acc[k][r] = 0;
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) {
+      const uint4 ql = q4[r * (D / 16) + j];           // query words 4j..4j+3 (dims 16j..)
+      const uint4 qh = q4[r * (D / 16) + D / 32 + j];  // words D/8+4j.. (dims D/2+16j..)
+      const uint32_t qlw[4] = {ql.x, ql.y, ql.z, ql.w}, qhw[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int i = 4 * j + t;
+          uint32_t lo = (w[k][i] << 4) & 0xF0F0F0F0u;  // 16*msb of dims 4i..4i+3
+          uint32_t hi = w[k][i] & 0xF0F0F0F0u;         // 16*msb of dims D/2+4i..
+          if (lw) {
+            lo |= lw[k][i] & 0x0F0F0F0Fu;
+            hi |= (lw[k][i] >> 4) & 0x0F0F0F0Fu;
+          }
+          acc[k][r] = dp4a(lo, qlw[t], acc[k][r]);
+          acc[k][r] = dp4a(hi, qhw[t], acc[k][r]);
+        }
       }
-      a = dp4a(lo, q[i], a);
-      a = dp4a(hi, q[D / 8 + i], a);
     }
-    acc[r] = a;
   }
 }
 
-// Block-wide (max, sum of exp2) of per-thread values for R heads, written
-// by thread 0 of the block to out[r*stride].
-template <int R>
-SPATTEN_DEV void block_stats(const float (&m)[R], const float (&l)[R], float* sh, float* out,
-                             int64_t stride) {
+template <int D, int K>
+SPATTEN_DEV void load_rows(const uint8_t* base, const int64_t (&key)[K], const bool (&ok)[K],
+                           uint32_t (&w)[K][D / 8]) {
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const uint4* src = reinterpret_cast<const uint4*>(base + (ok[k] ? key[k] : 0) * (D / 2));
+#pragma unroll
+    for (int i = 0; i < D / 32; ++i) {
+      const uint4 v = ok[k] ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
+      w[k][4 * i] = v.x; w[k][4 * i + 1] = v.y; w[k][4 * i + 2] = v.z; w[k][4 * i + 3] = v.w;
+    }
+  }
+}
+
+// Block-wide softmax statistics of K values per thread and head (-inf for
+// no key): the block max m_r, e[k][r] = exp2(s[k][r] - m_r) for the caller
+// and the sum l_r of the e; threads r < R write (m_r, l_r) to out[r*stride].
+// Max first, then one exp2 per value, then a sum: fixed reduction order.
+template <int R, int K>
+SPATTEN_DEV void block_softmax(const float (&s)[K][R], float* sh, float* out, int64_t stride,
+                               float (&e)[K][R]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  float* smax = sh;
+  float* ssum = sh + R * nw;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    float mm = m[r], ll = l[r];
+    float mm = s[0][r];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float mo = __shfl_xor_sync(0xffffffffu, mm, o);
-      const float lo = __shfl_xor_sync(0xffffffffu, ll, o);
-      const float mn = fmaxf(mm, mo);
-      ll = (mn == -INFINITY) ? 0.f : ll * exp2f(mm - mn) + lo * exp2f(mo - mn);
-      mm = mn;
+    for (int k = 1; k < K; ++k) mm = fmaxf(mm, s[k][r]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+    if (lane == 0) smax[r * nw + warp] = mm;
+  }
+  __syncthreads();
+  float mc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float m = -INFINITY;
+    for (int w = 0; w < nw; ++w) m = fmaxf(m, smax[r * nw + w]);
+    mc[r] = m;
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      e[k][r] = (m == -INFINITY) ? 0.f : fast_exp2(s[k][r] - m);
+      sum += e[k][r];
     }
-    if (lane == 0) {
-      sh[(r * nw + warp) * 2] = mm;
-      sh[(r * nw + warp) * 2 + 1] = ll;
-    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) ssum[r * nw + warp] = sum;
   }
   __syncthreads();
   if (threadIdx.x < R) {
     const int r = threadIdx.x;
-    float mm = -INFINITY, ll = 0.f;
-    for (int w = 0; w < nw; ++w) {
-      const float mo = sh[(r * nw + w) * 2], lo = sh[(r * nw + w) * 2 + 1];
-      const float mn = fmaxf(mm, mo);
-      ll = (mn == -INFINITY) ? 0.f : ll * exp2f(mm - mn) + lo * exp2f(mo - mn);
-      mm = mn;
-    }
-    out[r * stride] = mm;
-    out[r * stride + 1] = ll;
+    float l = 0.f;
+    for (int w = 0; w < nw; ++w) l += ssum[r * nw + w];
+    out[r * stride] = mc[r];
+    out[r * stride + 1] = l;
   }
 }
 
 // 1. MSB scores of every valid key for the R query heads of one KV head:
-// grid (chunks, G, B), one key per thread. scores [B, H, N] (log2 domain),
-// chunk statistics [B, H, chunks, 2].
+// grid (chunks of kScoreKeys, G, B), kKeysPerThread keys per thread (keys t
+// and t + kTok of the chunk: consecutive threads read consecutive rows).
+// scores [B, H, N] (log2 domain), chunk statistics [B, H, chunks, 2].
+constexpr int kKeysPerThread = 2;
+constexpr int kScoreKeys = kTok * kKeysPerThread;
+
 template <int D, int R>
 __global__ void __launch_bounds__(kTok) decode_scores_kernel(const DecodeParams p, float* scores,
                                                              float* part) {
-  __shared__ uint32_t qs[R * D / 4];
+  constexpr int K = kKeysPerThread;
+  __shared__ __align__(16) uint32_t qs[R * D / 4];
   __shared__ float cq[R];
   __shared__ float sh[R * (kTok / 32) * 2];
   const int b = blockIdx.z, g = blockIdx.y, chunk = blockIdx.x;
   for (int i = threadIdx.x; i < R * D / 4; i += blockDim.x)
     qs[i] = reinterpret_cast<const uint32_t*>(p.q8 + ((int64_t)b * p.H + g * R) * D)[i];
   if (threadIdx.x < R) cq[threadIdx.x] = p.q_scale[(int64_t)b * p.H + g * R + threadIdx.x] * p.sm_scale * kLog2e;
-  __syncthreads();
-  const int n = chunk * kTok + threadIdx.x;
-  float m[R], l[R];
+  int n[K];
+  int64_t key[K];
+  bool ok[K];
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    m[r] = -INFINITY;
-    l[r] = 0.f;
+  for (int k = 0; k < K; ++k) {
+    n[k] = chunk * kScoreKeys + k * kTok + threadIdx.x;
+    ok[k] = n[k] < p.n_valid;
+    key[k] = ((int64_t)b * p.G + g) * p.N + n[k];
   }
-  if (n < p.n_valid) {
-    const int64_t key = ((int64_t)b * p.G + g) * p.N + n;
-    uint32_t w[D / 8];
-    const uint4* src = reinterpret_cast<const uint4*>(p.k_msb + key * (D / 2));
+  uint32_t w[K][D / 8];
+  load_rows<D, K>(p.k_msb, key, ok, w);  // in flight while the query lands in smem
+  float ks[K];
 #pragma unroll
-    for (int i = 0; i < D / 32; ++i) {
-      const uint4 v = __ldg(src + i);
-      w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
-    }
-    const float ks = __ldg(p.k_scale + key);
-    int acc[R];
-    key_dots<D, R>(w, nullptr, qs, acc);
+  for (int k = 0; k < K; ++k) ks[k] = ok[k] ? __ldg(p.k_scale + key[k]) : 0.f;
+  __syncthreads();
+  int acc[K][R];
+  key_dots<D, R, K>(w, nullptr, qs, acc);
+  float sv[K][R];
+#pragma unroll
+  for (int k = 0; k < K; ++k)
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      const float s = (float)acc[r] * (cq[r] * ks);
-      scores[((int64_t)b * p.H + g * R + r) * p.N + n] = s;
-      m[r] = s;
-      l[r] = 1.f;
+      sv[k][r] = ok[k] ? (float)acc[k][r] * (cq[r] * ks[k]) : -INFINITY;
+      if (ok[k]) scores[((int64_t)b * p.H + g * R + r) * p.N + n[k]] = sv[k][r];
     }
-  }
   const int chunks = gridDim.x;
-  block_stats<R>(m, l, sh, part + (((int64_t)b * p.H + g * R) * chunks + chunk) * 2, (int64_t)chunks * 2);
+  float e[K][R];
+  block_softmax<R, K>(sv, sh, part + (((int64_t)b * p.H + g * R) * chunks + chunk) * 2, (int64_t)chunks * 2, e);
+}
+
+// 1b. global softmax statistics per (b, h) from the chunk statistics: a warp
+// per head; st [B, H, 2] = (max, 1 / sum).
+__global__ void __launch_bounds__(256) decode_stats_kernel(const DecodeParams p, const float* part, int chunks,
+                                                           float* st) {
+  const int lane = threadIdx.x & 31;
+  const int bh = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (bh >= p.B * p.H) return;
+  const float* pp = part + (int64_t)bh * chunks * 2;
+  float mm = -INFINITY;
+  for (int c = lane; c < chunks; c += 32) mm = fmaxf(mm, pp[2 * c]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+  float ll = 0.f;
+  if (mm != -INFINITY)
+    for (int c = lane; c < chunks; c += 32) ll += pp[2 * c + 1] * fast_exp2(pp[2 * c] - mm);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ll += __shfl_xor_sync(0xffffffffu, ll, o);
+  if (lane == 0) {
+    st[2 * bh] = mm;
+    st[2 * bh + 1] = ll > 0.f ? 1.f / ll : 0.f;
+  }
 }
 
 // 2. token importance = sum over the H heads of exp2(s - m_h) / l_h:
-// grid (ceil(N / 256), B); each CTA first reduces the chunk statistics.
+// grid (ceil(N / 256), B).
 __global__ void __launch_bounds__(256) decode_importance_kernel(const DecodeParams p, const float* scores,
-                                                                const float* part, int chunks) {
+                                                                const float* stg) {
   extern __shared__ float st[];  // [H][2]: m, 1/l
   const int b = blockIdx.y;
-  for (int h = threadIdx.x; h < p.H; h += blockDim.x) {
-    const float* pp = part + ((int64_t)b * p.H + h) * chunks * 2;
-    float mm = -INFINITY, ll = 0.f;
-    for (int c = 0; c < chunks; ++c) {
-      const float mo = pp[2 * c], lo = pp[2 * c + 1];
-      const float mn = fmaxf(mm, mo);
-      ll = (mn == -INFINITY) ? 0.f : ll * exp2f(mm - mn) + lo * exp2f(mo - mn);
-      mm = mn;
-    }
-    st[2 * h] = mm;
-    st[2 * h + 1] = ll > 0.f ? 1.f / ll : 0.f;
-  }
+  for (int i = threadIdx.x; i < 2 * p.H; i += blockDim.x) st[i] = stg[(int64_t)b * p.H * 2 + i];
   __syncthreads();
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= p.N) return;
   float imp = 0.f;
   if (n < p.n_valid) {
     for (int h = 0; h < p.H; ++h)
-      imp += exp2f(scores[((int64_t)b * p.H + h) * p.N + n] - st[2 * h]) * st[2 * h + 1];
+      imp += fast_exp2(scores[((int64_t)b * p.H + h) * p.N + n] - st[2 * h]) * st[2 * h + 1];
   }
   p.importance[(int64_t)b * p.N + n] = imp;
 }
@@ -186,7 +236,7 @@ __global__ void __launch_bounds__(256) decode_importance_kernel(const DecodePara
 template <int D, int R, typename T>
 __global__ void __launch_bounds__(kTok) decode_attend_kernel(const DecodeParams p, float* part_ml,
                                                              float* part_o) {
-  __shared__ uint32_t qs[R * D / 4];
+  __shared__ __align__(16) uint32_t qs[R * D / 4];
   __shared__ float cq[R];
   __shared__ float ps[R * kTok];  // exp2(s - m_split) per head and key
   __shared__ float sh[R * (kTok / 32) * 2];
@@ -201,43 +251,31 @@ __global__ void __launch_bounds__(kTok) decode_attend_kernel(const DecodeParams 
   const int n = have ? (int)p.kept[(int64_t)b * p.top_k + j] : -1;
   kidx[threadIdx.x] = n;
   __syncthreads();
-  float m[R], l[R], s[R];
+  float s[R];
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    m[r] = -INFINITY;
-    l[r] = 0.f;
-    s[r] = -INFINITY;
-  }
-  if (have && n >= 0 && n < p.n_valid) {
-    const int64_t key = ((int64_t)b * p.G + g) * p.N + n;
-    uint32_t w[D / 8], lw[D / 8];
-    const uint4* ms = reinterpret_cast<const uint4*>(p.k_msb + key * (D / 2));
-    const uint4* ls = reinterpret_cast<const uint4*>(p.k_lsb + key * (D / 2));
+  for (int r = 0; r < R; ++r) s[r] = -INFINITY;
+  {
+    const bool okk[1] = {have && n >= 0 && n < p.n_valid};
+    const int64_t key[1] = {((int64_t)b * p.G + g) * p.N + (okk[0] ? n : 0)};
+    uint32_t w[1][D / 8], lw[1][D / 8];
+    load_rows<D, 1>(p.k_msb, key, okk, w);
+    load_rows<D, 1>(p.k_lsb, key, okk, lw);
+    const float ks = okk[0] ? __ldg(p.k_scale + key[0]) : 0.f;
+    int acc[1][R];
+    key_dots<D, R, 1>(w, lw, qs, acc);
+    if (okk[0]) {
 #pragma unroll
-    for (int i = 0; i < D / 32; ++i) {
-      const uint4 a = __ldg(ms + i), c = __ldg(ls + i);
-      w[4 * i] = a.x; w[4 * i + 1] = a.y; w[4 * i + 2] = a.z; w[4 * i + 3] = a.w;
-      lw[4 * i] = c.x; lw[4 * i + 1] = c.y; lw[4 * i + 2] = c.z; lw[4 * i + 3] = c.w;
-    }
-    const float ks = __ldg(p.k_scale + key);
-    int acc[R];
-    key_dots<D, R>(w, lw, qs, acc);
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      s[r] = (float)acc[r] * (cq[r] * ks);
-      m[r] = s[r];
-      l[r] = 1.f;
+      for (int r = 0; r < R; ++r) s[r] = (float)acc[0][r] * (cq[r] * ks);
     }
   }
-  // split statistics -> sh_ml (thread 0 .. R-1 write them to part_ml)
+  // split statistics (max, sum) per head -> part_ml; exp2(s - max) -> ps
   float* ml = part_ml + (((int64_t)b * p.H + g * R) * splits + split) * 2;
-  block_stats<R>(m, l, sh, ml, (int64_t)splits * 2);
-  __syncthreads();
+  float sk[1][R], e[1][R];
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const float mr = ml[r * (int64_t)splits * 2];
-    ps[r * kTok + threadIdx.x] = (s[r] == -INFINITY) ? 0.f : exp2f(s[r] - mr);
-  }
+  for (int r = 0; r < R; ++r) sk[0][r] = s[r];
+  block_softmax<R, 1>(sk, sh, ml, (int64_t)splits * 2, e);
+#pragma unroll
+  for (int r = 0; r < R; ++r) ps[r * kTok + threadIdx.x] = e[0][r];
   __syncthreads();
   // phase 2: thread = (key group kg of 4, dim pair dp of D/2)
   const int dp = threadIdx.x % (D / 2), kg = threadIdx.x / (D / 2);
@@ -247,10 +285,11 @@ __global__ void __launch_bounds__(kTok) decode_attend_kernel(const DecodeParams 
   for (int r = 0; r < R; ++r) o[r][0] = o[r][1] = 0.f;
   const T* vb = static_cast<const T*>(p.v) + ((int64_t)b * p.G + g) * p.N * D;
   const int cnt = min(kTok, p.top_k - split * kTok);
+#pragma unroll 4
   for (int t = kg; t < cnt; t += kGroups) {
     const int nn = kidx[t];
-    if (nn < 0 || nn >= p.n_valid) continue;
-    const float2 vv = load2<T>(vb + (int64_t)nn * D + 2 * dp);
+    const bool okv = nn >= 0 && nn < p.n_valid;
+    const float2 vv = okv ? load2<T>(vb + (int64_t)nn * D + 2 * dp) : make_float2(0.f, 0.f);
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const float pr = ps[r * kTok + t];
@@ -293,12 +332,15 @@ __global__ void decode_combine_kernel(const DecodeParams p, const float* part_ml
 
 template <int D, int R>
 cudaError_t importance_d(const DecodeParams& p, const DecodeWorkspace& w, cudaStream_t st) {
-  const int chunks = (p.n_valid + kTok - 1) / kTok;
+  const int chunks = (p.n_valid + kScoreKeys - 1) / kScoreKeys;
   decode_scores_kernel<D, R><<<dim3(chunks, p.G, p.B), kTok, 0, st>>>(p, w.scores, w.part);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  decode_stats_kernel<<<(p.B * p.H + 7) / 8, 256, 0, st>>>(p, w.part, chunks, w.st);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
   decode_importance_kernel<<<dim3((p.N + 255) / 256, p.B), 256, p.H * 2 * sizeof(float), st>>>(p, w.scores,
-                                                                                               w.part, chunks);
+                                                                                               w.st);
   return cudaGetLastError();
 }
 
@@ -316,10 +358,11 @@ cudaError_t attend_dt(const DecodeParams& p, const DecodeWorkspace& w, cudaStrea
 
 DecodeWorkspaceSizes decode_workspace_sizes(const DecodeParams& p) {
   DecodeWorkspaceSizes s;
-  const int chunks = (p.n_valid + kTok - 1) / kTok;
+  const int chunks = (p.n_valid + kScoreKeys - 1) / kScoreKeys;
   const int splits = (p.top_k + kTok - 1) / kTok;
   s.scores = (size_t)p.B * p.H * p.N * sizeof(float);
   s.part = (size_t)p.B * p.H * (chunks > 0 ? chunks : 1) * 2 * sizeof(float);
+  s.st = (size_t)p.B * p.H * 2 * sizeof(float);
   s.ml = (size_t)p.B * p.H * (splits > 0 ? splits : 1) * 2 * sizeof(float);
   s.o = (size_t)p.B * p.H * (splits > 0 ? splits : 1) * p.D * sizeof(float);
   return s;

@@ -26,12 +26,13 @@ struct DecodeParams {
 struct DecodeWorkspace {
   float* scores;  // [B, H, N]
   float* part;    // [B, H, chunks, 2]
+  float* st;      // [B, H, 2]
   float* ml;      // [B, H, splits, 2]
   float* o;       // [B, H, splits, D]
 };
 
 struct DecodeWorkspaceSizes {
-  size_t scores, part, ml, o;
+  size_t scores, part, st, ml, o;
 };
 
 DecodeWorkspaceSizes decode_workspace_sizes(const DecodeParams& p);
