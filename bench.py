@@ -64,6 +64,8 @@ def parse():
     ap.add_argument("--no-decode", action="store_true", help="skip the Qwen3 decode measurement")
     ap.add_argument("--only-decode", action="store_true",
                     help="run only the Qwen3 decode attention (--steps timed steps) and print its line")
+    ap.add_argument("--decode-batch", type=int, default=64,
+                    help="batch of the Qwen3 decode measurement (64; smaller for profiling captures)")
     ap.add_argument("--only-qwen3", action="store_true",
                     help="run only the Qwen3 prefill (--steps timed prefills) and print its line")
     return ap.parse_args()
@@ -444,7 +446,7 @@ def qwen3_bench(torch, dev, steps=3, warmup=2):
 DEC_B, DEC_H, DEC_G, DEC_N, DEC_D, DEC_TOPK, DEC_LAYERS = 64, 32, 8, 32768, 128, 2048, 36
 
 
-def decode_bench(torch, rank, world, dev, steps=3):
+def decode_bench(torch, rank, world, dev, steps=3, batch=DEC_B):
     """Qwen3-8B-architecture decode attention (32 Q heads, 8 KV heads,
     head_dim 128, 36 layers), bf16, batch 64, a KV cache of 32768 tokens with
     K / V drawn N(0,1) from seed 0, K as 4-bit MSB / LSB planes, top-k keeps
@@ -457,11 +459,11 @@ def decode_bench(torch, rank, world, dev, steps=3):
     from spatten_b200.decode import decode_attention, quant_kv_cache
     G, H = DEC_G // world, DEC_H // world
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    k = torch.randn(DEC_B, G, DEC_N, DEC_D, generator=g, device=dev, dtype=torch.bfloat16)
-    cache = quant_kv_cache(k, torch.randn(DEC_B, G, DEC_N, DEC_D, generator=g, device=dev,
+    k = torch.randn(batch, G, DEC_N, DEC_D, generator=g, device=dev, dtype=torch.bfloat16)
+    cache = quant_kv_cache(k, torch.randn(batch, G, DEC_N, DEC_D, generator=g, device=dev,
                                           dtype=torch.bfloat16))
     del k
-    qs = [torch.randn(DEC_B, H, DEC_D, generator=g, device=dev, dtype=torch.bfloat16)
+    qs = [torch.randn(batch, H, DEC_D, generator=g, device=dev, dtype=torch.bfloat16)
           for _ in range(DEC_LAYERS)]
     grp = dist.group.WORLD if world > 1 else None
     st = torch.cuda.current_stream(dev)
@@ -488,14 +490,14 @@ def decode_bench(torch, rank, world, dev, steps=3):
         ms = float(t.item())
     # algorithmic bytes of one layer at one rank: the MSB plane and scale of
     # every cached key; both planes, the scale and V of every kept key; q, out
-    per_layer = (DEC_B * G * DEC_N * (DEC_D // 2 + 4) + DEC_B * G * DEC_TOPK * (DEC_D + 2 * DEC_D + 4)
-                 + 2 * DEC_B * H * DEC_D * 2)
+    per_layer = (batch * G * DEC_N * (DEC_D // 2 + 4) + batch * G * DEC_TOPK * (DEC_D + 2 * DEC_D + 4)
+                 + 2 * batch * H * DEC_D * 2)
     layer_ms = ms / DEC_LAYERS
     del cache, qs
     torch.cuda.empty_cache()
-    return {"ms_per_step": ms, "tokens_per_s": DEC_B / (ms * 1e-3), "layer_ms": layer_ms,
+    return {"ms_per_step": ms, "tokens_per_s": batch / (ms * 1e-3), "layer_ms": layer_ms,
             "hbm_gbs_per_gpu": per_layer / (layer_ms * 1e-3) / 1e9, "algorithmic_bytes_per_layer_gpu": per_layer,
-            "batch": DEC_B, "cache_len": DEC_N, "top_k": DEC_TOPK, "layers": DEC_LAYERS,
+            "batch": batch, "cache_len": DEC_N, "top_k": DEC_TOPK, "layers": DEC_LAYERS,
             "kv_heads_per_gpu": G, "dtype": "bf16",
             "config": "Qwen3-8B decode attention: 32 Q / 8 KV heads, head_dim 128, K/V N(0,1), K as "
                       "4-bit planes, importance all-reduced over KV-head shards, top-2048 per step"}
@@ -720,7 +722,7 @@ def main():
         try:
             dev = torch.device("cuda", local_rank)
             torch.cuda.set_device(dev)
-            d = decode_bench(torch, rank, world, dev, steps=args.steps)
+            d = decode_bench(torch, rank, world, dev, steps=args.steps, batch=args.decode_batch)
             if rank == 0:
                 print(json.dumps(dict(metric="qwen3_decode_tokens_per_s", value=d["tokens_per_s"],
                                       unit="tokens/s", higher_is_better=True, n_gpus=world, **d)), flush=True)

@@ -24,6 +24,12 @@ SPATTEN_DEV void cp_async16(void* smem, const void* gmem, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)),
                "l"(gmem), "r"(src_bytes));
 }
+// 4-byte asynchronous global->shared copy (through L1); `valid` = false zero-fills.
+SPATTEN_DEV void cp_async4(void* smem, const void* gmem, bool valid) {
+  int src_bytes = valid ? 4 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(smem_u32(smem)),
+               "l"(gmem), "r"(src_bytes));
+}
 SPATTEN_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 SPATTEN_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }

@@ -32,6 +32,7 @@ def _case(B, H, G, N, D, dt, seed):
     (2, 8, 1, 1500, 128, 257, None, torch.bfloat16),
     (2, 4, 4, 700, 64, 100, 650, torch.float16),
     (1, 16, 2, 2048, 128, 2048, None, torch.bfloat16),
+    (1, 32, 8, 16384, 128, 2048, 16000, torch.bfloat16),
 ])
 def test_decode_matches_oracle(B, H, G, N, D, top_k, n_valid, dt):
     from spatten_b200.decode import _quant_query, decode_attention, quant_kv_cache
