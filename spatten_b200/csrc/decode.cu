@@ -15,8 +15,10 @@
 //      (the LSB plane is fetched for the kept keys only), softmax, P.V, in
 //      token splits whose partial (max, sum, output) are combined at the end
 //      (decode_attend + decode_combine).
-// All of it is byte / integer work bound by HBM: CUDA cores with dp4a,
-// coalesced 16-byte loads, no tensor cores.
+// All of it is bound by HBM: the only contraction is q (R <= 8 heads of a
+// GQA group) against the keys, done as int8 mma.m16n8k32 tiles with the
+// operands expanded in registers from the packed nibbles; the gathers and
+// the plane stream are cp.async copies into shared memory.
 #include <climits>
 
 #include "common.cuh"
@@ -26,10 +28,7 @@
 namespace spatten {
 namespace {
 
-constexpr int kTok = 256;   // keys per CTA in the score and attend kernels
-constexpr int kMaxR = 8;    // query heads per KV head (GQA group)
-
-SPATTEN_DEV int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
+constexpr int kTok = 256;  // threads of the score kernel, keys per ring stage
 
 // eight consecutive 16-bit values (one 16-byte load) as floats
 template <typename T>
@@ -51,57 +50,6 @@ SPATTEN_DEV void unpack8<__nv_bfloat16>(const uint4& u, float (&f)[8]) {
   for (int i = 0; i < 4; ++i) {
     f[2 * i] = __uint_as_float(w[i] << 16);
     f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-  }
-}
-
-// Exact int scores of K keys for R heads. w[k] holds key k's packed plane
-// words (D/8 words of the MSB plane; byte p = dim p | dim p+D/2 << 4); with
-// `lw` the LSB plane's, for the full int8 key k8 = 16*msb + lsb. The query
-// words of head r sit at qs[r*D/4 ..] in shared memory, read 16 bytes at a
-// time and shared by the K keys.
-template <int D, int R, int K>
-SPATTEN_DEV void key_dots(const uint32_t (&w)[K][D / 8], const uint32_t (*lw)[D / 8], const uint32_t* qs,
-                          int (&acc)[K][R]) {
-  const uint4* q4 = reinterpret_cast<const uint4*>(qs);
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-#pragma unroll
-    for (int k = 0; k < K; ++k) acc[k][r] = 0;
-#pragma unroll
-    for (int j = 0; j < D / 32; ++j) {
-      const uint4 ql = q4[r * (D / 16) + j];           // query words 4j..4j+3 (dims 16j..)
-      const uint4 qh = q4[r * (D / 16) + D / 32 + j];  // words D/8+4j.. (dims D/2+16j..)
-      const uint32_t qlw[4] = {ql.x, ql.y, ql.z, ql.w}, qhw[4] = {qh.x, qh.y, qh.z, qh.w};
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int i = 4 * j + t;
-          uint32_t lo = (w[k][i] << 4) & 0xF0F0F0F0u;  // 16*msb of dims 4i..4i+3
-          uint32_t hi = w[k][i] & 0xF0F0F0F0u;         // 16*msb of dims D/2+4i..
-          if (lw) {
-            lo |= lw[k][i] & 0x0F0F0F0Fu;
-            hi |= (lw[k][i] >> 4) & 0x0F0F0F0Fu;
-          }
-          acc[k][r] = dp4a(lo, qlw[t], acc[k][r]);
-          acc[k][r] = dp4a(hi, qhw[t], acc[k][r]);
-        }
-      }
-    }
-  }
-}
-
-template <int D, int K>
-SPATTEN_DEV void load_rows(const uint8_t* base, const int64_t (&key)[K], const bool (&ok)[K],
-                           uint32_t (&w)[K][D / 8]) {
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const uint4* src = reinterpret_cast<const uint4*>(base + (ok[k] ? key[k] : 0) * (D / 2));
-#pragma unroll
-    for (int i = 0; i < D / 32; ++i) {
-      const uint4 v = ok[k] ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
-      w[k][4 * i] = v.x; w[k][4 * i + 1] = v.y; w[k][4 * i + 2] = v.z; w[k][4 * i + 3] = v.w;
-    }
   }
 }
 
@@ -381,75 +329,150 @@ __global__ void __launch_bounds__(256) decode_importance_kernel(const DecodePara
   p.importance[(int64_t)b * p.N + n] = imp;
 }
 
-// 3. exact attention over the kept keys, in splits of kTok keys: grid
-// (splits, G, B). The V rows of the split's kept keys are requested first
-// (cp.async into shared memory) so that their gather overlaps phase 1.
-// Phase 1: one kept key per thread, full int8 scores for the R heads ->
-// smem; split max / sum per head. Phase 2: P.V out of shared memory, a lane
-// per 8 dims of a row; the per-warp partial outputs are then summed in the
-// (by then free) V buffer.
+// 3. exact attention over the kept keys, in splits of kAttKeys keys: grid
+// (splits, G, B), kAttKeys threads. The split's kept rows are gathered with
+// cp.async into shared memory at once: both K planes and the scales (first
+// group) and the V rows (second group, in flight during phase 1).
+// Phase 1: exact int8 scores q8 . k8 on the tensor cores (mma.m16n8k32 s8,
+// A = k8 = 16*msb + lsb expanded in registers from the two packed planes,
+// B = the R query heads padded to 8), then the split's softmax per head
+// (max, sum -> part_ml; exp2(s - max) -> ps). Phase 2: P.V out of shared
+// memory, a lane per 8 dims of a row; the per-warp partial outputs are then
+// summed in the (by then free) V buffer.
+constexpr int kAttKeys = 128;
+
 template <int D>
-__host__ __device__ constexpr size_t attend_smem_bytes() {
-  return (size_t)kTok * D * 2;  // V rows, 16-bit
+struct AttendLayout {
+  static constexpr int RB = D / 2;
+  static constexpr int oMsb = 0;                          // [kAttKeys][RB], 16-byte chunks swizzled
+  static constexpr int oLsb = oMsb + kAttKeys * RB;       // same
+  static constexpr int oV = oLsb + kAttKeys * RB;         // [kAttKeys][D] 16-bit
+  static constexpr int oScale = oV + kAttKeys * D * 2;    // [kAttKeys]
+  static constexpr int kBytes = oScale + kAttKeys * 4;
+};
+
+// R consecutive floats from shared memory (16-byte aligned for R >= 4)
+template <int R>
+SPATTEN_DEV void load_heads(const float* src, float (&f)[R]) {
+  if constexpr (R >= 4) {
+#pragma unroll
+    for (int i = 0; i < R / 4; ++i) {
+      const float4 v = reinterpret_cast<const float4*>(src)[i];
+      f[4 * i] = v.x; f[4 * i + 1] = v.y; f[4 * i + 2] = v.z; f[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < R; ++i) f[i] = src[i];
+  }
 }
 
 template <int D, int R, typename T>
-__global__ void __launch_bounds__(kTok) decode_attend_kernel(const DecodeParams p, float* part_ml,
-                                                             float* part_o) {
-  constexpr int LPR = D / 8, RPW = 32 / LPR, NW = kTok / 32;  // 16-byte chunks per V row
-  static_assert(NW * R * D * sizeof(float) <= attend_smem_bytes<D>(), "partial outputs fit the V buffer");
+__global__ void __launch_bounds__(kAttKeys) decode_attend_kernel(const DecodeParams p, float* part_ml,
+                                                                 float* part_o) {
+  static_assert(R <= 8, "one n8 tile of query heads");
+  using L = AttendLayout<D>;
+  constexpr int RB = L::RB, CH = RB / 16, NWD = D / 32, NW = kAttKeys / 32;
+  constexpr int LPR = D / 8, RPW = 32 / LPR;  // 16-byte chunks per V row, V rows per warp step
+  static_assert(NW * R * D * sizeof(float) <= (size_t)kAttKeys * D * 2, "partial outputs fit the V buffer");
   extern __shared__ __align__(128) uint8_t dsm[];
-  uint4* vs = reinterpret_cast<uint4*>(dsm);  // [kTok][LPR]
-  __shared__ __align__(16) uint32_t qs[R * D / 4];
-  __shared__ float cq[R];
-  __shared__ float ps[R * kTok];  // exp2(s - m_split) per head and key
-  __shared__ float sh[R * (kTok / 32) * 2];
-  __shared__ int kidx[kTok];
+  uint8_t* msb = dsm + L::oMsb;
+  uint8_t* lsb = dsm + L::oLsb;
+  uint4* vs = reinterpret_cast<uint4*>(dsm + L::oV);
+  float* ksm = reinterpret_cast<float*>(dsm + L::oScale);
+  __shared__ __align__(16) float ps[kAttKeys * R];  // [key][head]: scores, then exp2(s - m_split)
+  __shared__ float cq[8];
+  __shared__ float sh[R * NW * 2];
+  __shared__ int kidx[kAttKeys];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gq = lane >> 2, tq = lane & 3;
   const int b = blockIdx.z, g = blockIdx.y, split = blockIdx.x, splits = gridDim.x;
-  for (int i = threadIdx.x; i < R * D / 4; i += blockDim.x)
-    qs[i] = reinterpret_cast<const uint32_t*>(p.q8 + ((int64_t)b * p.H + g * R) * D)[i];
-  if (threadIdx.x < R) cq[threadIdx.x] = p.q_scale[(int64_t)b * p.H + g * R + threadIdx.x] * p.sm_scale * kLog2e;
-  const int j = split * kTok + threadIdx.x;  // position in the kept list
+  if (tid < 8) cq[tid] = tid < R ? p.q_scale[(int64_t)b * p.H + g * R + tid] * p.sm_scale * kLog2e : 0.f;
+  const int j = split * kAttKeys + tid;  // position in the kept list
   const int64_t nk = j < p.top_k ? p.kept[(int64_t)b * p.top_k + j] : -1;
   const int n = (nk >= 0 && nk < p.n_valid) ? (int)nk : -1;  // -1: no key
-  kidx[threadIdx.x] = n;
+  kidx[tid] = n;
   __syncthreads();
-  const T* vb = static_cast<const T*>(p.v) + ((int64_t)b * p.G + g) * p.N * D;
-  const int cnt = min(kTok, p.top_k - split * kTok);
-  for (int c = threadIdx.x; c < cnt * LPR; c += kTok) {
+  const int64_t bgN = ((int64_t)b * p.G + g) * p.N;
+  const int cnt = min(kAttKeys, p.top_k - split * kAttKeys);
+  for (int c = tid; c < kAttKeys * CH; c += kAttKeys) {
+    const int t = c / CH, col = c % CH, nn = kidx[t];
+    const int64_t row = bgN + (nn >= 0 ? nn : 0);
+    const int off = t * RB + ((col ^ row_swizzle<D>(t)) << 4);
+    cp_async16(msb + off, p.k_msb + row * RB + col * 16, nn >= 0);
+    cp_async16(lsb + off, p.k_lsb + row * RB + col * 16, nn >= 0);
+  }
+  cp_async4(ksm + tid, p.k_scale + bgN + (n >= 0 ? n : 0), n >= 0);
+  cp_async_commit();
+  const T* vb = static_cast<const T*>(p.v) + bgN * D;
+  for (int c = tid; c < cnt * LPR; c += kAttKeys) {
     const int t = c / LPR, dc = c % LPR, nn = kidx[t];
     cp_async16(vs + c, vb + (int64_t)(nn >= 0 ? nn : 0) * D + dc * 8, nn >= 0);
   }
   cp_async_commit();
-  float s[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) s[r] = -INFINITY;
+  // B fragments: head gq (zero beyond R), dims 32kk + 4tq .. and 32kk + 16 + 4tq ..
+  uint32_t qb[NWD][2];
   {
-    const bool okk[1] = {n >= 0};
-    const int64_t key[1] = {((int64_t)b * p.G + g) * p.N + (n >= 0 ? n : 0)};
-    uint32_t w[1][D / 8], lw[1][D / 8];
-    load_rows<D, 1>(p.k_msb, key, okk, w);
-    load_rows<D, 1>(p.k_lsb, key, okk, lw);
-    const float ks = okk[0] ? __ldg(p.k_scale + key[0]) : 0.f;
-    int acc[1][R];
-    key_dots<D, R, 1>(w, lw, qs, acc);
-    if (okk[0]) {
+    const uint32_t* qw = reinterpret_cast<const uint32_t*>(p.q8 + ((int64_t)b * p.H + g * R + (gq < R ? gq : 0)) * D);
 #pragma unroll
-      for (int r = 0; r < R; ++r) s[r] = (float)acc[0][r] * (cq[r] * ks);
+    for (int kk = 0; kk < NWD; ++kk) {
+      qb[kk][0] = gq < R ? __ldg(qw + 8 * kk + tq) : 0u;
+      qb[kk][1] = gq < R ? __ldg(qw + 8 * kk + 4 + tq) : 0u;
     }
   }
-  // split statistics (max, sum) per head -> part_ml; exp2(s - max) -> ps
-  float* ml = part_ml + (((int64_t)b * p.H + g * R) * splits + split) * 2;
-  float sk[1][R], e[1][R];
+  cp_async_wait<1>();
+  __syncthreads();
+  // phase 1: warp w scores keys 32w .. 32w+31 of the split (two 16-key tiles)
+  const int h0 = 2 * tq, h1 = 2 * tq + 1;
 #pragma unroll
-  for (int r = 0; r < R; ++r) sk[0][r] = s[r];
-  block_softmax<R, 1>(sk, sh, ml, (int64_t)splits * 2, e);
+  for (int grp = 0; grp < 2; ++grp) {
+    const int r0 = warp * 32 + grp * 16 + gq, r1 = r0 + 8;
+    uint32_t m0[NWD], l0[NWD], m1[NWD], l1[NWD];
 #pragma unroll
-  for (int r = 0; r < R; ++r) ps[r * kTok + threadIdx.x] = e[0][r];
+    for (int jj = 0; jj < NWD; ++jj) {
+      const int o0 = r0 * RB + ((jj ^ row_swizzle<D>(r0)) << 4) + 4 * tq;
+      const int o1 = r1 * RB + ((jj ^ row_swizzle<D>(r1)) << 4) + 4 * tq;
+      m0[jj] = *reinterpret_cast<const uint32_t*>(msb + o0);
+      l0[jj] = *reinterpret_cast<const uint32_t*>(lsb + o0);
+      m1[jj] = *reinterpret_cast<const uint32_t*>(msb + o1);
+      l1[jj] = *reinterpret_cast<const uint32_t*>(lsb + o1);
+    }
+    // k8 = 16*msb + lsb of 4 dims: low nibbles for the first D/2 dims, high after
+    auto full = [](uint32_t mw, uint32_t lw, bool hi) -> uint32_t {
+      return hi ? ((mw & 0xF0F0F0F0u) | ((lw >> 4) & 0x0F0F0F0Fu))
+                : (((mw << 4) & 0xF0F0F0F0u) | (lw & 0x0F0F0F0Fu));
+    };
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int kk = 0; kk < NWD; ++kk) {
+      const bool hi = kk >= NWD / 2;
+      const int jj = 2 * (hi ? kk - NWD / 2 : kk);
+      const uint32_t a[4] = {full(m0[jj], l0[jj], hi), full(m1[jj], l1[jj], hi), full(m0[jj + 1], l0[jj + 1], hi),
+                             full(m1[jj + 1], l1[jj + 1], hi)};
+      mma_s8_16832(acc, a, qb[kk][0], qb[kk][1]);
+    }
+    const float ka = ksm[r0], kb = ksm[r1];
+    const bool va = kidx[r0] >= 0, vb2 = kidx[r1] >= 0;
+    if (h0 < R) {
+      ps[r0 * R + h0] = va ? (float)acc[0] * (cq[h0] * ka) : -INFINITY;
+      ps[r1 * R + h0] = vb2 ? (float)acc[2] * (cq[h0] * kb) : -INFINITY;
+    }
+    if (h1 < R) {
+      ps[r0 * R + h1] = va ? (float)acc[1] * (cq[h1] * ka) : -INFINITY;
+      ps[r1 * R + h1] = vb2 ? (float)acc[3] * (cq[h1] * kb) : -INFINITY;
+    }
+  }
+  __syncthreads();
+  // the split's statistics (max, sum) per head -> part_ml; exp2(s - max) -> ps
+  {
+    float* ml = part_ml + (((int64_t)b * p.H + g * R) * splits + split) * 2;
+    float sk[1][R], e[1][R];
+    load_heads<R>(ps + tid * R, sk[0]);
+    block_softmax<R, 1>(sk, sh, ml, (int64_t)splits * 2, e);
+#pragma unroll
+    for (int r = 0; r < R; ++r) ps[tid * R + r] = e[0][r];
+  }
   cp_async_wait<0>();
   __syncthreads();
   // phase 2: lane = (key row slot rs, 8-dim chunk dc)
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int dc = lane % LPR, rs = lane / LPR;
   float o[R][8];
 #pragma unroll
@@ -458,14 +481,13 @@ __global__ void __launch_bounds__(kTok) decode_attend_kernel(const DecodeParams 
     for (int jj = 0; jj < 8; ++jj) o[r][jj] = 0.f;
 #pragma unroll 4
   for (int t = warp * RPW + rs; t < cnt; t += NW * RPW) {
-    float vv[8];
+    float vv[8], pr[R];
     unpack8<T>(vs[t * LPR + dc], vv);
+    load_heads<R>(ps + t * R, pr);
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const float pr = ps[r * kTok + t];
+    for (int r = 0; r < R; ++r)
 #pragma unroll
-      for (int jj = 0; jj < 8; ++jj) o[r][jj] = fmaf(pr, vv[jj], o[r][jj]);
-    }
+      for (int jj = 0; jj < 8; ++jj) o[r][jj] = fmaf(pr[r], vv[jj], o[r][jj]);
   }
 #pragma unroll
   for (int r = 0; r < R; ++r)
@@ -475,7 +497,7 @@ __global__ void __launch_bounds__(kTok) decode_attend_kernel(const DecodeParams 
       for (int off = LPR; off < 32; off <<= 1) o[r][jj] += __shfl_xor_sync(0xffffffffu, o[r][jj], off);
     }
   __syncthreads();  // every warp is done with the V rows
-  float* red = reinterpret_cast<float*>(dsm);  // [NW][R][D]
+  float* red = reinterpret_cast<float*>(dsm + L::oV);  // [NW][R][D]
   if (rs == 0) {
 #pragma unroll
     for (int r = 0; r < R; ++r)
@@ -483,7 +505,7 @@ __global__ void __launch_bounds__(kTok) decode_attend_kernel(const DecodeParams 
       for (int jj = 0; jj < 8; ++jj) red[(warp * R + r) * D + dc * 8 + jj] = o[r][jj];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < R * D; i += blockDim.x) {
+  for (int i = tid; i < R * D; i += blockDim.x) {
     float a = 0.f;
 #pragma unroll
     for (int w = 0; w < NW; ++w) a += red[w * R * D + i];
@@ -531,12 +553,12 @@ cudaError_t importance_d(const DecodeParams& p, const DecodeWorkspace& w, cudaSt
 
 template <int D, int R, typename T>
 cudaError_t attend_dt(const DecodeParams& p, const DecodeWorkspace& w, cudaStream_t st) {
-  const int splits = (p.top_k + kTok - 1) / kTok;
-  constexpr size_t smem = attend_smem_bytes<D>();
+  const int splits = (p.top_k + kAttKeys - 1) / kAttKeys;
+  constexpr size_t smem = AttendLayout<D>::kBytes;
   cudaError_t e = cudaFuncSetAttribute(decode_attend_kernel<D, R, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
-  decode_attend_kernel<D, R, T><<<dim3(splits, p.G, p.B), kTok, smem, st>>>(p, w.ml, w.o);
+  decode_attend_kernel<D, R, T><<<dim3(splits, p.G, p.B), kAttKeys, smem, st>>>(p, w.ml, w.o);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   decode_combine_kernel<T><<<dim3(p.H, p.B), D, 0, st>>>(p, w.ml, w.o, splits);
@@ -548,7 +570,7 @@ cudaError_t attend_dt(const DecodeParams& p, const DecodeWorkspace& w, cudaStrea
 DecodeWorkspaceSizes decode_workspace_sizes(const DecodeParams& p) {
   DecodeWorkspaceSizes s;
   const int chunks = (p.n_valid + kCtaKeys - 1) / kCtaKeys;
-  const int splits = (p.top_k + kTok - 1) / kTok;
+  const int splits = (p.top_k + kAttKeys - 1) / kAttKeys;
   s.scores = (size_t)p.B * p.H * p.N * sizeof(float);
   s.part = (size_t)p.B * p.H * (chunks > 0 ? chunks : 1) * 2 * sizeof(float);
   s.st = (size_t)p.B * p.H * 2 * sizeof(float);
