@@ -328,7 +328,11 @@ def bert_bench(torch, rank, world, dev, steps=5):
     from transformers import BertConfig, BertModel
     from spatten_b200.bert import patch_bert
     torch.manual_seed(0)
-    model = BertModel(BertConfig(attn_implementation="eager")).half().to(dev).eval()
+    # The attention core is the drop-in's in either case; "sdpa" only selects
+    # HF's mask builder, which for an unpadded batch passes no mask at all
+    # (the "eager" builder materialises an additive [B, 1, S, S] zero mask
+    # every forward, from a host-made scalar that graph capture rejects).
+    model = BertModel(BertConfig(attn_implementation="sdpa")).half().to(dev).eval()
     knobs = dict(BERT_KNOBS)
     if world > 1:
         knobs["process_group"] = dist.group.WORLD
@@ -358,31 +362,47 @@ def bert_bench(torch, rank, world, dev, steps=5):
         if world > 1:
             dist.barrier()
         eager_ms = timed(lambda: model(input_ids=ids, attention_mask=mask))
-        # One rank: the whole cascade forward as one CUDA graph (the kept
-        # token and head counts follow from the ratios, so every shape is
-        # static; the kept indices stay on the device).
+        # The whole cascade forward as one CUDA graph (the kept token and
+        # head counts follow from the ratios, so every shape is static; the
+        # kept indices stay on the device). With several ranks the graph
+        # holds the per-layer head-importance all-reduce; every rank captures
+        # and replays the same number of times.
         graph_ms = None
         graph_error = None
-        if world == 1:
-            try:
-                side = torch.cuda.Stream(dev)
-                side.wait_stream(st)
-                with torch.cuda.stream(side):
-                    model(input_ids=ids, attention_mask=mask)
-                st.wait_stream(side)
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g):
-                    out_g = model(input_ids=ids, attention_mask=mask).last_hidden_state
-                g.replay()
-                torch.cuda.synchronize(dev)
-                if torch.equal(out_g, ref):
-                    graph_ms = timed(g.replay)
-                else:
-                    graph_error = "graph output differs from the eager forward"
-                del g
-            except RuntimeError as err:
-                graph_ms = None
-                graph_error = str(err).splitlines()[0][:200]
+        g = None
+        try:
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(st)
+            with torch.cuda.stream(side):
+                model(input_ids=ids, attention_mask=mask)
+            st.wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                out_g = model(input_ids=ids, attention_mask=mask).last_hidden_state
+        except RuntimeError as err:
+            g = None
+            graph_error = str(err).splitlines()[0][:200]
+        ok = g is not None
+        if world > 1:  # every rank replays its graph (and its all-reduces), or none does
+            f = torch.tensor([1.0 if ok else 0.0], device=dev)
+            dist.all_reduce(f, op=dist.ReduceOp.MIN)
+            ok = bool(f.item() > 0)
+        if ok:
+            g.replay()
+            torch.cuda.synchronize(dev)
+            same = torch.equal(out_g, ref)
+            if world > 1:
+                f = torch.tensor([1.0 if same else 0.0], device=dev)
+                dist.all_reduce(f, op=dist.ReduceOp.MIN)
+                same = bool(f.item() > 0)
+            if same:
+                graph_ms = timed(g.replay)
+            else:
+                graph_error = "graph output differs from the eager forward"
+        elif graph_error is None:
+            graph_error = "graph capture failed on another rank"
+        del g
+        torch.cuda.synchronize(dev)
     ms = eager_ms if graph_ms is None else graph_ms
     if world > 1:
         t = torch.tensor([ms], device=dev)
