@@ -6,9 +6,12 @@
 //   msb = x8 >> 4 (signed nibble), lsb = x8 & 15, x8 == 16*msb + lsb.
 // Packing: byte p of a row holds dim p (low nibble) and dim p + D/2 (high).
 //
-// HBM-bound: one warp per row, each lane owns D/32 consecutive dims; the row
-// max is a warp reduction. Reads 2*D (fp16) bytes and writes D (+4) bytes per
-// row; the grid is a grid-stride loop sized to the SM count.
+// HBM-bound. Rows whose start is 16-byte aligned (the usual case: contiguous
+// tensors and the strided Q/K views of a fused QKV GEMM output) take the
+// vector kernel, D / (16 / sizeof(T)) lanes per row with one 16-byte load
+// each; others take a warp per row, each lane owning D/32 consecutive dims.
+// Reads 2*D (fp16) bytes and writes D (+4) bytes per row; the grid is a
+// grid-stride loop sized to the SM count.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -80,6 +83,111 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
   }
 }
 
+// Vector variant for rows whose start is 16-byte aligned (every row when the
+// base and the strides are): LPR = D / (16 / sizeof(T)) lanes per row, each
+// with one 16-byte load of EPL consecutive elements, 32 / LPR rows per warp
+// step; the row max is a reduction over the row's lanes, and the quantised
+// bytes leave in one 4- or 8-byte store per lane. Same arithmetic as above.
+template <typename T, int D, bool PLANES>
+__global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict__ x, int Z, int H,
+                                                             int M, int64_t sz, int64_t sh,
+                                                             int64_t sm, int8_t* __restrict__ q8,
+                                                             uint8_t* __restrict__ msb,
+                                                             uint8_t* __restrict__ lsb,
+                                                             float* __restrict__ scale) {
+  constexpr int EPL = 16 / sizeof(T);  // elements per lane
+  constexpr int LPR = D / EPL;         // lanes per row
+  constexpr int RPW = 32 / LPR;        // rows per warp step
+  constexpr int NWORD = EPL / 4;       // packed int8 words per lane
+  static_assert(LPR >= 2 && LPR <= 32 && 32 % LPR == 0, "row must span 2..32 lanes");
+  const int lane = threadIdx.x & 31, sub = lane / LPR, li = lane % LPR;
+  const int64_t rows = (int64_t)Z * H * M;
+  const int64_t step = (int64_t)gridDim.x * (blockDim.x >> 5) * RPW;
+  for (int64_t r0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW; r0 < rows;
+       r0 += step) {
+    const int64_t r = r0 + sub;
+    const bool live = r < rows;
+    float v[EPL];
+    if (live) {
+      const int64_t m = r % M, zh = r / M;
+      const int64_t h = zh % H, z = zh / H;
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + z * sz + h * sh + m * sm) + li);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) v[i] = to_f32<T>(e[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) v[i] = 0.f;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float s = __fdiv_rn(amax, 127.0f);
+    uint32_t w[NWORD];
+#pragma unroll
+    for (int k = 0; k < NWORD; ++k) {
+      uint32_t packed = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        int t = 0;
+        if (s != 0.f) {
+          t = __float2int_rn(__fdiv_rn(v[4 * k + b], s));
+          t = max(-127, min(127, t));
+        }
+        packed |= ((uint32_t)t & 0xFFu) << (8 * b);
+      }
+      w[k] = packed;
+    }
+    if (live && li == 0) scale[r] = s;
+    if (!PLANES) {
+      if (live) {
+        int8_t* dst = q8 + r * D + li * EPL;
+        if constexpr (NWORD == 2) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+        else *reinterpret_cast<uint32_t*>(dst) = w[0];
+      }
+    } else {
+      // lane li < LPR/2 holds dims [li*EPL, +EPL) = the low nibbles of those
+      // bytes; lane li + LPR/2 holds the dims D/2 above (the high nibbles)
+      uint32_t hw[NWORD];
+#pragma unroll
+      for (int k = 0; k < NWORD; ++k) hw[k] = __shfl_down_sync(0xffffffffu, w[k], LPR / 2);
+      if (live && li < LPR / 2) {
+        uint32_t pm[NWORD], pl[NWORD];
+#pragma unroll
+        for (int k = 0; k < NWORD; ++k) {
+          pm[k] = ((w[k] >> 4) & 0x0F0F0F0Fu) | (hw[k] & 0xF0F0F0F0u);
+          pl[k] = (w[k] & 0x0F0F0F0Fu) | ((hw[k] & 0x0F0F0F0Fu) << 4);
+        }
+        uint8_t* dm = msb + r * (D / 2) + li * EPL;
+        uint8_t* dl = lsb + r * (D / 2) + li * EPL;
+        if constexpr (NWORD == 2) {
+          *reinterpret_cast<uint2*>(dm) = make_uint2(pm[0], pm[1]);
+          *reinterpret_cast<uint2*>(dl) = make_uint2(pl[0], pl[1]);
+        } else {
+          *reinterpret_cast<uint32_t*>(dm) = pm[0];
+          *reinterpret_cast<uint32_t*>(dl) = pl[0];
+        }
+      }
+    }
+  }
+}
+
+template <typename T, int D, bool PLANES>
+static cudaError_t launch_quant_vec(const T* x, int Z, int H, int M, int64_t sz, int64_t sh, int64_t sm,
+                                    int8_t* q8, uint8_t* msb, uint8_t* lsb, float* scale, cudaStream_t st,
+                                    int64_t blocks) {
+  constexpr int LPR = D / (16 / (int)sizeof(T));
+  if constexpr (LPR >= 2 && LPR <= 32) {
+    quant_rows_vec_kernel<T, D, PLANES><<<(unsigned)blocks, 256, 0, st>>>(x, Z, H, M, sz, sh, sm, q8, msb,
+                                                                          lsb, scale);
+    return cudaGetLastError();
+  } else {
+    return cudaErrorInvalidValue;
+  }
+}
+
 template <typename T, bool PLANES>
 static cudaError_t launch_quant_t(const void* x, int Z, int H, int M, int D, int64_t sz,
                                   int64_t sh, int64_t sm, int8_t* q8, uint8_t* msb, uint8_t* lsb,
@@ -91,6 +199,22 @@ static cudaError_t launch_quant_t(const void* x, int Z, int H, int M, int D, int
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   const T* xp = static_cast<const T*>(x);
+  const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (sz * (int64_t)sizeof(T)) % 16 == 0 &&
+                   (sh * (int64_t)sizeof(T)) % 16 == 0 && (sm * (int64_t)sizeof(T)) % 16 == 0;
+  constexpr int EPL = 16 / sizeof(T);
+  if (vec && D >= 2 * EPL && D <= 32 * EPL) {
+    const int rpw = 32 / (D / EPL);
+    int64_t vblocks = (rows + 8 * rpw - 1) / (8 * rpw);
+    if (vblocks > cap) vblocks = cap;
+    if (vblocks < 1) vblocks = 1;
+    switch (D) {
+      case 32: return launch_quant_vec<T, 32, PLANES>(xp, Z, H, M, sz, sh, sm, q8, msb, lsb, scale, st, vblocks);
+      case 64: return launch_quant_vec<T, 64, PLANES>(xp, Z, H, M, sz, sh, sm, q8, msb, lsb, scale, st, vblocks);
+      case 128: return launch_quant_vec<T, 128, PLANES>(xp, Z, H, M, sz, sh, sm, q8, msb, lsb, scale, st, vblocks);
+      case 256: return launch_quant_vec<T, 256, PLANES>(xp, Z, H, M, sz, sh, sm, q8, msb, lsb, scale, st, vblocks);
+      default: return cudaErrorInvalidValue;
+    }
+  }
 #define SPATTEN_QL(E)                                                                        \
   quant_rows_kernel<T, E, PLANES><<<(unsigned)blocks, threads, 0, st>>>(xp, Z, H, M, sz, sh, \
                                                                         sm, q8, msb, lsb, scale)
