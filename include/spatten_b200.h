@@ -30,6 +30,10 @@
  *       torch.gather of hidden states / cumulative scores on the token axis
  *       (module.py:53-54, 62-63) and torch.index_select of head rows of the
  *       Q/K/V weights (module.py:22-28).
+ *   spatten_qkv_proj
+ *       slice_linear_weights (module.py:12-34) + the Q/K/V projections of
+ *       SpattenBertSelfAttention.forward (spatten_bert.py:72-78) + the K
+ *       plane split (spatten_bert_ultimate.py:184-185), in one kernel.
  */
 #ifndef SPATTEN_B200_H
 #define SPATTEN_B200_H
@@ -207,6 +211,55 @@ int spatten_decode_importance(const spatten_decode_args* a, void* workspace, siz
                               void* stream);
 int spatten_decode_attend(const spatten_decode_args* a, void* workspace, size_t workspace_bytes,
                           void* stream);
+
+/*
+ * Fused Q/K/V projection of the active heads, with the quantisation the
+ * attention kernel reads. Replaces, per layer of the cascade:
+ *   slice_linear_weights (module.py:12-34): index_select of the active heads'
+ *     rows of W_q, W_k, W_v and their biases -- no copy here: the weight
+ *     tiles are loaded from the full weight at the active heads' rows;
+ *   the projections q/k/v = F.linear(hidden, W_sliced, b_sliced)
+ *     (spatten_bert.py:72-78);
+ *   the K plane split (spatten_bert_ultimate.py:184-185), made integer, and
+ *     the int8 query, as spatten_quant_q_int8 / spatten_quant_k_planes would
+ *     compute them from the rounded projections.
+ * x [B*S, Kdim] (row t = b*S + s, row stride x_row_stride elements); w
+ * [3*Hall*Dh, Kdim] contiguous, the Q rows, then the K rows, then the V rows
+ * (nn.Linear layout, the reference's query/key/value weights stacked); bias
+ * [3*Hall*Dh] or NULL; heads [cur] int64 weight head of each active slot
+ * (NULL: 0 .. cur-1). dtype f16 or bf16 for x, w, bias and the fp outputs.
+ * Outputs are head-major, [B, cur, S, ...] contiguous:
+ *   mode SPATTEN_PROJ_QUANT: q8 [.., Dh] int8 + q_scale [B, cur, S];
+ *     k_msb, k_lsb [.., Dh/2] + k_scale [B, cur, S]; v [.., Dh];
+ *   mode SPATTEN_PROJ_DENSE: q, k, v [.., Dh].
+ * Dh in {64, 128}; Kdim a multiple of 8; x, w and every output 16-byte
+ * aligned. The GEMM accumulates in fp32 on the tensor cores, adds the bias
+ * and rounds to dtype before quantising (the values an unfused projection
+ * stores; its accumulation order may differ in the last bit).
+ */
+#define SPATTEN_PROJ_QUANT 0
+#define SPATTEN_PROJ_DENSE 1
+typedef struct {
+  int dtype;
+  int mode;
+  int B, S, Kdim;
+  int Hall, Dh, cur;
+  const void* x;
+  int64_t x_row_stride;
+  const void* w;
+  const void* bias;
+  const int64_t* heads;
+  int8_t* q8;
+  float* q_scale;
+  uint8_t* k_msb;
+  uint8_t* k_lsb;
+  float* k_scale;
+  void* q;
+  void* k;
+  void* v;
+} spatten_qkv_proj_args;
+
+int spatten_qkv_proj(const spatten_qkv_proj_args* a, void* stream);
 
 /*
  * Top-k selection, indices returned in ascending order:

@@ -16,6 +16,7 @@ ERR_UNSUPPORTED = 3
 
 DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
 MODE_QUANT, MODE_DENSE, MODE_COMPAT = 0, 1, 2
+PROJ_QUANT, PROJ_DENSE = 0, 1
 
 ABI_VERSION = 3
 MAX_V_PRUNE_COUNT = 8  # spatten_prog_attn_args.v_prune_count limit
@@ -57,6 +58,17 @@ class DecodeArgs(ctypes.Structure):
     ]
 
 
+class QkvProjArgs(ctypes.Structure):
+    """Mirror of spatten_qkv_proj_args (include/spatten_b200.h)."""
+    _fields_ = [
+        ("dtype", c_int), ("mode", c_int), ("B", c_int), ("S", c_int), ("Kdim", c_int),
+        ("Hall", c_int), ("Dh", c_int), ("cur", c_int),
+        ("x", c_vp), ("x_row_stride", c_i64), ("w", c_vp), ("bias", c_vp), ("heads", c_vp),
+        ("q8", c_vp), ("q_scale", c_vp), ("k_msb", c_vp), ("k_lsb", c_vp), ("k_scale", c_vp),
+        ("q", c_vp), ("k", c_vp), ("v", c_vp),
+    ]
+
+
 # name -> (restype, argtypes); every entry point declared in include/spatten_b200.h
 SIGNATURES = {
     "spatten_abi_version": (c_int, []),
@@ -74,6 +86,7 @@ SIGNATURES = {
     "spatten_decode_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(DecodeArgs)]),
     "spatten_decode_importance": (c_int, [ctypes.POINTER(DecodeArgs), c_vp, ctypes.c_size_t, c_vp]),
     "spatten_decode_attend": (c_int, [ctypes.POINTER(DecodeArgs), c_vp, ctypes.c_size_t, c_vp]),
+    "spatten_qkv_proj": (c_int, [ctypes.POINTER(QkvProjArgs), c_vp]),
     "spatten_gather_rows": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_int, c_int, c_int,
                                     c_i64, c_i64, c_vp, c_i64, c_i64, c_vp]),
 }

@@ -29,10 +29,12 @@ every row, ties to the smaller key index).
 ``quant_threshold`` is the row max-probability below which a row's LSB plane
 is refetched (the reference used it as a tile logit bound).
 
-On CUDA every step runs through libspatten_b200: head-row weight gather, one
-cuBLAS GEMM for the selected Q/K/V rows, int8/4-bit quantisation, the fused
-attention (mask, softmax, V prune, P.V, importance, scatter into the
-full-width context), and the radix-select top-k for heads and tokens. There is
+On CUDA every step runs through libspatten_b200: for fp16 / bf16 models one
+tensor-core kernel projects the active heads' Q/K/V straight from the full
+weight (no slicing copy) and quantises Q and K in its epilogue (fp32 models:
+head-row weight gather, one library GEMM, the quantisation kernels); then the
+fused attention (mask, softmax, V prune, P.V, importance, scatter into the
+full-width context) and the radix-select top-k for heads and tokens. There is
 no CPU path: a CPU module raises.
 """
 import math
@@ -45,6 +47,7 @@ from transformers.models.bert.modeling_bert import BertEncoder, BertSelfAttentio
 
 from . import _native as N
 from .progressive import prog_attn, quant_k_planes, quant_q_int8
+from .proj import qkv_proj
 from .select import gather_head_rows, gather_rows, topk_indices
 
 
@@ -142,16 +145,23 @@ class SpattenBertSelfAttention(BertSelfAttention):
         if heads is None:
             heads = torch.arange(H, device=dev)
         cur = heads.numel()
-        # head-row gather of the concatenated Q/K/V weights, one GEMM
         w, b = self._qkv_params()
-        rows = torch.cat([heads, heads + H, heads + 2 * H])
-        wsel = gather_head_rows(w, rows, d)
-        bsel = gather_head_rows(b, rows, d)
-        qkv = F.linear(hidden_states, wsel, bsel)          # [B, S, 3*cur*d]
-        qkv4 = qkv.view(B, S, 3, cur, d)
-        q = qkv4[:, :, 0].permute(0, 2, 1, 3)              # [B, cur, S, d] strided views
-        k = qkv4[:, :, 1].permute(0, 2, 1, 3)
-        v = qkv4[:, :, 2].permute(0, 2, 1, 3)
+        fused = hidden_states.dtype in (torch.float16, torch.bfloat16) and d in (64, 128)
+        if fused:
+            # one tensor-core kernel: the active heads' weight tiles read in
+            # place (no slicing copy), Q / K quantised in its epilogue
+            pr = qkv_proj(hidden_states, w, b, H, d, heads=heads, quantize=self.enable_prog_quant)
+            v = pr.v                                       # [B, cur, S, d]
+        else:
+            # head-row gather of the concatenated Q/K/V weights, one GEMM
+            rows = torch.cat([heads, heads + H, heads + 2 * H])
+            wsel = gather_head_rows(w, rows, d)
+            bsel = gather_head_rows(b, rows, d)
+            qkv = F.linear(hidden_states, wsel, bsel)      # [B, S, 3*cur*d]
+            qkv4 = qkv.view(B, S, 3, cur, d)
+            q = qkv4[:, :, 0].permute(0, 2, 1, 3)          # [B, cur, S, d] strided views
+            k = qkv4[:, :, 1].permute(0, 2, 1, 3)
+            v = qkv4[:, :, 2].permute(0, 2, 1, 3)
         bias = _mask_bias(attention_mask, B, S)
         v_thr, v_count = 0.0, 0
         if self.enable_v_prune:
@@ -172,13 +182,18 @@ class SpattenBertSelfAttention(BertSelfAttention):
                       want_tok=True, want_head=True, out=full.permute(0, 2, 1, 3),
                       out_head_map=heads, out_head_slots=H)
         if self.enable_prog_quant:
-            q8, qs = quant_q_int8(q)
-            kp = quant_k_planes(k)
+            if fused:
+                q8, qs, kp = pr.q8, pr.q_scale, pr.k_planes
+            else:
+                q8, qs = quant_q_int8(q)
+                kp = quant_k_planes(k)
             r = prog_attn(q8, kp.msb, v, k1=kp.lsb, mode=N.MODE_QUANT, q_scale=qs,
                           k_scale=kp.scale, refetch_thr=float(self.quant_threshold),
                           want_refetch=True, **common)
             self.last_refetch = r.refetch
         else:
+            if fused:
+                q, k = pr.q, pr.k
             r = prog_attn(q, k, v, mode=N.MODE_DENSE, **common)
         if self.process_group is not None:
             from .distributed import allreduce_head_importance

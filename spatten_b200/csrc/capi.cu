@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "decode.h"
 #include "kernels.h"
+#include "proj.h"
 
 namespace {
 
@@ -83,7 +84,11 @@ const char* spatten_last_error(void) { return g_err.c_str(); }
 
 int spatten_device_error(unsigned int* code, int reset) {
   if (!code) return fail(SPATTEN_ERR_INVALID, "device_error: null output");
-  return cuda_status(spatten::read_device_error(code, reset != 0), "device_error read");
+  unsigned int proj = 0;
+  if (int e = cuda_status(spatten::read_device_error(code, reset != 0), "device_error read")) return e;
+  if (int e = cuda_status(spatten::read_proj_device_error(&proj, reset != 0), "device_error read")) return e;
+  if (*code == 0) *code = proj;
+  return ok();
 }
 
 int spatten_quant_q_int8(const void* x, int dtype, int Z, int H, int M, int D, int64_t sz,
@@ -344,6 +349,47 @@ int spatten_decode_attend(const spatten_decode_args* a, void* workspace, size_t 
   spatten::DecodeWorkspace w;
   if (int e = decode_workspace(p, workspace, workspace_bytes, w)) return e;
   return cuda_status(spatten::launch_decode_attend(p, w, (cudaStream_t)stream), "decode attend launch");
+}
+
+int spatten_qkv_proj(const spatten_qkv_proj_args* a, void* stream) {
+  if (!a) return fail(SPATTEN_ERR_INVALID, "qkv_proj: null args");
+  if (a->dtype != SPATTEN_DTYPE_F16 && a->dtype != SPATTEN_DTYPE_BF16)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "qkv_proj: dtype %d (need f16 or bf16)", a->dtype);
+  if (a->mode != SPATTEN_PROJ_QUANT && a->mode != SPATTEN_PROJ_DENSE)
+    return fail(SPATTEN_ERR_INVALID, "qkv_proj: mode %d", a->mode);
+  if (a->B < 1 || a->S < 1 || a->Kdim < 1 || a->Hall < 1 || a->cur < 1 || a->cur > a->Hall)
+    return fail(SPATTEN_ERR_INVALID, "qkv_proj: bad sizes B=%d S=%d Kdim=%d Hall=%d cur=%d", a->B, a->S,
+                a->Kdim, a->Hall, a->cur);
+  if (a->Dh != 64 && a->Dh != 128) return fail(SPATTEN_ERR_UNSUPPORTED, "qkv_proj: Dh=%d (need 64 or 128)", a->Dh);
+  if ((int64_t)a->B * a->S > (int64_t)1 << 30 || (int64_t)3 * a->Hall * a->Dh > (int64_t)1 << 30)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "qkv_proj: too many rows");
+  if (a->Kdim % 8) return fail(SPATTEN_ERR_UNSUPPORTED, "qkv_proj: Kdim %d not a multiple of 8", a->Kdim);
+  if (a->x_row_stride < a->Kdim || a->x_row_stride % 8)
+    return fail(SPATTEN_ERR_INVALID, "qkv_proj: x row stride %lld (need >= Kdim, multiple of 8)",
+                (long long)a->x_row_stride);
+  if (!a->x || !a->w || !a->v) return fail(SPATTEN_ERR_INVALID, "qkv_proj: null x/w/v");
+  if (!aligned(a->x, 16) || !aligned(a->w, 16) || !aligned(a->v, 16) || (a->bias && !aligned(a->bias, 2)) ||
+      (a->heads && !aligned(a->heads, 8)))
+    return fail(SPATTEN_ERR_INVALID, "qkv_proj: x/w/v not 16-byte aligned or bias/heads misaligned");
+  if (a->mode == SPATTEN_PROJ_QUANT) {
+    if (!a->q8 || !a->q_scale || !a->k_msb || !a->k_lsb || !a->k_scale)
+      return fail(SPATTEN_ERR_INVALID, "qkv_proj: null quantised output");
+    if (!aligned(a->q8, 16) || !aligned(a->k_msb, 16) || !aligned(a->k_lsb, 16) || !aligned(a->q_scale, 4) ||
+        !aligned(a->k_scale, 4))
+      return fail(SPATTEN_ERR_INVALID, "qkv_proj: quantised outputs misaligned");
+  } else {
+    if (!a->q || !a->k) return fail(SPATTEN_ERR_INVALID, "qkv_proj: null q/k");
+    if (!aligned(a->q, 16) || !aligned(a->k, 16)) return fail(SPATTEN_ERR_INVALID, "qkv_proj: q/k misaligned");
+  }
+  spatten::ProjParams p;
+  p.dtype = a->dtype;
+  p.mode = a->mode;
+  p.B = a->B; p.S = a->S; p.Kdim = a->Kdim;
+  p.Hall = a->Hall; p.Dh = a->Dh; p.cur = a->cur;
+  p.x = a->x; p.x_st = a->x_row_stride; p.w = a->w; p.bias = a->bias; p.heads = a->heads;
+  p.q8 = a->q8; p.q_scale = a->q_scale; p.k_msb = a->k_msb; p.k_lsb = a->k_lsb; p.k_scale = a->k_scale;
+  p.q = a->q; p.k = a->k; p.v = a->v;
+  return cuda_status(spatten::launch_qkv_proj(p, (cudaStream_t)stream), "qkv_proj launch");
 }
 
 }  // extern "C"

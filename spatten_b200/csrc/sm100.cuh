@@ -12,9 +12,10 @@ namespace sm100 {
 
 // ---------------------------------------------------------------------------
 // Device error word: a kernel whose wait runs out of time records where it gave
-// up here (first writer wins) and returns instead of spinning forever. This
-// header is included by one translation unit (prog_attn_tc.cu), which also
-// reads the word back for spatten_device_error().
+// up here (first writer wins) and returns instead of spinning forever. The
+// word is static: each translation unit that includes this header
+// (prog_attn_tc.cu, qkv_proj.cu) has its own and reads it back for
+// spatten_device_error().
 // ---------------------------------------------------------------------------
 static __device__ unsigned int g_device_error = 0;
 
@@ -96,6 +97,13 @@ SPATTEN_DEV void tma_load_4d(void* smem_dst, const CUtensorMap* map, int c0, int
       " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
       "r"(smem_u32(bar))
+      : "memory");
+}
+SPATTEN_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
       : "memory");
 }
 SPATTEN_DEV void prefetch_tmap(const CUtensorMap* map) {

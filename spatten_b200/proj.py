@@ -1,0 +1,90 @@
+"""Fused Q/K/V projection of the active heads (host side of spatten_qkv_proj).
+
+One tensor-core kernel replaces, per layer of the cascade, the reference's
+``slice_linear_weights`` (module.py:12-34: index_select of the active heads'
+rows of W_q / W_k / W_v and their biases), the three projections of
+``SpattenBertSelfAttention.forward`` (spatten_bert.py:72-78) and the
+quantisation of Q and K that the progressive attention reads (the K plane
+split of spatten_bert_ultimate.py:184-185, made integer). The weight is never
+sliced: the kernel loads its tiles from the active heads' rows of the full
+stacked weight.
+
+``qkv_proj(x, w, bias, num_heads, head_dim, heads=None, quantize=True)``
+    x     [B, S, Kdim] fp16 / bf16 (rows contiguous)
+    w     [3 * num_heads * head_dim, Kdim]: the query, key and value weights
+          stacked (nn.Linear layout)
+    bias  [3 * num_heads * head_dim] or None
+    heads int64 [cur] active heads (None: all)
+returns ``QkvQuant(q8, q_scale, k_planes, v)`` (quantize=True: Q int8 +
+scale, K as 4-bit MSB / LSB planes + scale) or ``QkvDense(q, k, v)``; every
+output head-major [B, cur, S, ...], as the attention kernel reads them.
+"""
+from typing import NamedTuple
+
+import torch
+
+from . import _native as N
+from .progressive import _DT, KPlanes, _stream
+
+
+class QkvQuant(NamedTuple):
+    q8: torch.Tensor       # int8 [B, cur, S, Dh]
+    q_scale: torch.Tensor  # fp32 [B, cur, S]
+    k_planes: KPlanes      # uint8 [B, cur, S, Dh/2] x 2, fp32 [B, cur, S]
+    v: torch.Tensor        # [B, cur, S, Dh]
+
+
+class QkvDense(NamedTuple):
+    q: torch.Tensor  # [B, cur, S, Dh]
+    k: torch.Tensor
+    v: torch.Tensor
+
+
+def qkv_proj(x, w, bias, num_heads, head_dim, heads=None, quantize=True):
+    if not (x.is_cuda and w.is_cuda):
+        raise ValueError("qkv_proj takes CUDA tensors; there is no CPU path")
+    if x.dtype not in (torch.float16, torch.bfloat16) or w.dtype != x.dtype:
+        raise ValueError("qkv_proj: x and w must both be fp16 or both bf16")
+    if x.dim() != 3:
+        raise ValueError(f"qkv_proj: x must be [B, S, Kdim], got {tuple(x.shape)}")
+    B, S, Kdim = x.shape
+    if x.stride(2) != 1 or x.stride(0) != S * x.stride(1):
+        x = x.contiguous()
+    w = w.contiguous()
+    if tuple(w.shape) != (3 * num_heads * head_dim, Kdim):
+        raise ValueError(f"qkv_proj: w must be [{3 * num_heads * head_dim}, {Kdim}], got {tuple(w.shape)}")
+    if bias is not None:
+        bias = bias.contiguous()
+        if bias.dtype != x.dtype or bias.numel() != w.shape[0]:
+            raise ValueError("qkv_proj: bias must match w's rows and x's dtype")
+    if heads is not None:
+        heads = heads.to(torch.int64).contiguous()
+        cur = heads.numel()
+    else:
+        cur = num_heads
+    dev, dt = x.device, x.dtype
+    a = N.QkvProjArgs()
+    a.dtype = _DT[dt]
+    a.mode = N.PROJ_QUANT if quantize else N.PROJ_DENSE
+    a.B, a.S, a.Kdim = B, S, Kdim
+    a.Hall, a.Dh, a.cur = num_heads, head_dim, cur
+    a.x, a.x_row_stride = x.data_ptr(), x.stride(1)
+    a.w = w.data_ptr()
+    a.bias = None if bias is None else bias.data_ptr()
+    a.heads = None if heads is None else heads.data_ptr()
+    v = torch.empty((B, cur, S, head_dim), dtype=dt, device=dev)
+    a.v = v.data_ptr()
+    if quantize:
+        q8 = torch.empty((B, cur, S, head_dim), dtype=torch.int8, device=dev)
+        qs = torch.empty((B, cur, S), dtype=torch.float32, device=dev)
+        msb = torch.empty((B, cur, S, head_dim // 2), dtype=torch.uint8, device=dev)
+        lsb = torch.empty_like(msb)
+        ks = torch.empty((B, cur, S), dtype=torch.float32, device=dev)
+        a.q8, a.q_scale, a.k_msb, a.k_lsb, a.k_scale = (t.data_ptr() for t in (q8, qs, msb, lsb, ks))
+        N.check(N.lib.spatten_qkv_proj(a, _stream(x)))
+        return QkvQuant(q8, qs, KPlanes(msb, lsb, ks), v)
+    q = torch.empty_like(v)
+    k = torch.empty_like(v)
+    a.q, a.k = q.data_ptr(), k.data_ptr()
+    N.check(N.lib.spatten_qkv_proj(a, _stream(x)))
+    return QkvDense(q, k, v)

@@ -169,3 +169,25 @@ def test_decode_args_validation():
     assert N.lib.spatten_decode_importance(a, None, 0, None) == N.ERR_UNSUPPORTED
     a.H, a.n_valid = 8, 1001
     assert N.lib.spatten_decode_attend(a, None, 0, None) == N.ERR_INVALID
+
+
+def test_qkv_proj_args_validation():
+    """The fused projection rejects bad arguments before any launch."""
+    from spatten_b200 import _native as N
+    assert N.lib.spatten_qkv_proj(None, None) == N.ERR_INVALID
+    a = N.QkvProjArgs()
+    a.dtype, a.mode, a.B, a.S, a.Kdim, a.Hall, a.Dh, a.cur = N.DTYPE_F16, N.PROJ_QUANT, 2, 100, 768, 12, 64, 11
+    a.x = a.w = a.v = 1 << 20
+    a.x_row_stride = 768
+    assert N.lib.spatten_qkv_proj(a, None) == N.ERR_INVALID  # quantised outputs missing
+    a.q8 = a.q_scale = a.k_msb = a.k_lsb = a.k_scale = 1 << 21
+    a.dtype = N.DTYPE_F32
+    assert N.lib.spatten_qkv_proj(a, None) == N.ERR_UNSUPPORTED
+    a.dtype, a.Dh = N.DTYPE_BF16, 96
+    assert N.lib.spatten_qkv_proj(a, None) == N.ERR_UNSUPPORTED
+    a.Dh, a.cur = 64, 13  # more active heads than the weight has
+    assert N.lib.spatten_qkv_proj(a, None) == N.ERR_INVALID
+    a.cur, a.x_row_stride = 11, 700
+    assert N.lib.spatten_qkv_proj(a, None) == N.ERR_INVALID
+    a.x_row_stride, a.x = 768, (1 << 20) + 8  # x not 16-byte aligned
+    assert N.lib.spatten_qkv_proj(a, None) == N.ERR_INVALID
