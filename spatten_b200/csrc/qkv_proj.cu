@@ -47,9 +47,9 @@ namespace {
 using namespace sm100;
 
 constexpr int PM = 128;  // tokens per tile (TMEM lanes)
-constexpr int PN = 128;  // output columns per tile (TMEM columns of one accumulator)
+constexpr int PN = 256;  // output columns per tile (TMEM columns of one accumulator)
 constexpr int PK = 64;   // K step: 64 elements = one 128-byte swizzle atom
-constexpr int kStages = 6;
+constexpr int kStages = 4;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 2 * PN;
@@ -64,7 +64,7 @@ struct ProjLayout {
   static constexpr int kNumBars = 2 * kStages + 5;
   static constexpr int oTmem = oBar + kNumBars * 8;
   static constexpr int oAbort = oTmem + 4;
-  static constexpr int oBias = oAbort + 12;                  // float [kEpiWarps][128] per-warp bias copy
+  static constexpr int oBias = oAbort + 12;                  // float [kEpiWarps][128] per-warp bias copy (one head)
   static constexpr int kBytes = oBias + kEpiWarps * 128 * 4;
   static constexpr int kAlloc = kBytes + 1024;
 };
@@ -107,46 +107,41 @@ SPATTEN_DEV int quant_div(float x, float sc, float rc) {
   return (int)t;
 }
 
-// Epilogue of one tile for one token row (TMEM lane r of accumulator `tl`)
-// and warp half `half`: at Dh = 64 head `half` of the tile, at Dh = 128
-// columns [half * 64, half * 64 + 64) of its one head (the row max still
-// covers the whole head). Values are the rounded activations acc + bias;
-// `sb` is this warp's shared-memory copy of the head's bias (Dh floats).
+// Epilogue of one head of a tile for one token row (TMEM lane r; `tl` is
+// the accumulator's lane base): head hc of the tile, all Dh of its columns.
+// Values are the rounded activations acc + bias; `sb` is this warp's
+// shared-memory copy of the head's bias (Dh floats).
 template <typename T>
-SPATTEN_DEV void epilogue_tile(const ProjParams& p, uint32_t tl, const Tile& tl_, int r, int half, int T_,
+SPATTEN_DEV void epilogue_head(const ProjParams& p, uint32_t tl, const Tile& tl_, int r, int hc, int T_,
                                float* sb) {
   const int Dh = p.Dh, lane = threadIdx.x & 31;
   const int tok = tl_.m0 + r;
   const bool valid = tok < T_;
   const int b = valid ? tok / p.S : 0, s = valid ? tok % p.S : 0;
-  const int hc = Dh == 64 ? half : 0;        // head of the tile
   const int hs = (tl_.col0 + hc * Dh) / Dh;  // active slot
-  if (hs >= p.cur) return;                   // padding half of the last tile (warp-uniform)
+  if (hs >= p.cur) return;                   // padding of the last tile (warp-uniform)
   const int cb = hc * Dh;                    // first accumulator column of the head
-  const int c_lo = Dh == 64 ? 0 : half * 64;  // this half's columns within the head
   const int64_t orow = ((int64_t)b * p.cur + hs) * p.S + s;
   {
     const T* bias = static_cast<const T*>(p.bias);
     const int64_t bcol = (int64_t)tl_.which * p.Hall * Dh + (int64_t)head_of(p, hs) * Dh;
-    __syncwarp();  // the previous tile's reads of sb are done
+    __syncwarp();  // the previous head's reads of sb are done
     for (int c = lane; c < Dh; c += 32) sb[c] = bias ? to_f32<T>(__ldg(bias + bcol + c)) : 0.f;
     __syncwarp();
   }
   const bool quant = p.mode == 0 && tl_.which < 2;
   if (!quant) {
     T* dst = static_cast<T*>(tl_.which == 2 ? p.v : (tl_.which == 0 ? p.q : p.k)) + orow * Dh;
-#pragma unroll
-    for (int cc = 0; cc < 64; cc += 32) {
+    for (int cc = 0; cc < Dh; cc += 32) {
       uint32_t a[32];
-      tmem_ld32(tl + cb + c_lo + cc, a);
+      tmem_ld32(tl + cb + cc, a);
       tmem_wait_ld();
       if (valid) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i)
-          pk[i] = pack2<T>(__uint_as_float(a[2 * i]) + sb[c_lo + cc + 2 * i],
-                           __uint_as_float(a[2 * i + 1]) + sb[c_lo + cc + 2 * i + 1]);
-        uint4* d4 = reinterpret_cast<uint4*>(dst + c_lo + cc);
+          pk[i] = pack2<T>(__uint_as_float(a[2 * i]) + sb[cc + 2 * i], __uint_as_float(a[2 * i + 1]) + sb[cc + 2 * i + 1]);
+        uint4* d4 = reinterpret_cast<uint4*>(dst + cc);
 #pragma unroll
         for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
@@ -175,46 +170,45 @@ SPATTEN_DEV void epilogue_tile(const ProjParams& p, uint32_t tl, const Tile& tl_
   };
   if (tl_.which == 0) {
     int8_t* dst = p.q8 + orow * Dh;
-#pragma unroll
-    for (int cc = 0; cc < 64; cc += 32) {
+    for (int cc = 0; cc < Dh; cc += 32) {
       uint32_t a[32];
-      tmem_ld32(tl + cb + c_lo + cc, a);
+      tmem_ld32(tl + cb + cc, a);
       tmem_wait_ld();
       uint32_t w[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) w[j] = q4(a, 4 * j, c_lo + cc + 4 * j);
+      for (int j = 0; j < 8; ++j) w[j] = q4(a, 4 * j, cc + 4 * j);
       if (valid) {
-        uint4* d4 = reinterpret_cast<uint4*>(dst + c_lo + cc);
+        uint4* d4 = reinterpret_cast<uint4*>(dst + cc);
         d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
         d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
       }
     }
-    if (valid && half == hc) p.q_scale[orow] = sc;  // one writer per (row, head)
+    if (valid) p.q_scale[orow] = sc;
   } else {
-    // packed byte p = dim p (low nibble) | dim p + Dh/2 (high nibble); this
-    // half packs the 32 bytes from p_lo
-    const int pp = Dh == 64 ? 0 : half * 32;
-    uint32_t lo[32], hi[32];
-    tmem_ld32(tl + cb + pp, lo);
-    tmem_ld32(tl + cb + Dh / 2 + pp, hi);
-    tmem_wait_ld();
-    uint32_t wm[8], wl[8];
+    // packed byte p = dim p (low nibble) | dim p + Dh/2 (high nibble)
+    for (int pp = 0; pp < Dh / 2; pp += 32) {
+      uint32_t lo[32], hi[32];
+      tmem_ld32(tl + cb + pp, lo);
+      tmem_ld32(tl + cb + Dh / 2 + pp, hi);
+      tmem_wait_ld();
+      uint32_t wm[8], wl[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t L = q4(lo, 4 * j, pp + 4 * j);
-      const uint32_t H = q4(hi, 4 * j, Dh / 2 + pp + 4 * j);
-      wm[j] = ((L >> 4) & 0x0F0F0F0Fu) | (H & 0xF0F0F0F0u);
-      wl[j] = (L & 0x0F0F0F0Fu) | ((H & 0x0F0F0F0Fu) << 4);
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t L = q4(lo, 4 * j, pp + 4 * j);
+        const uint32_t H = q4(hi, 4 * j, Dh / 2 + pp + 4 * j);
+        wm[j] = ((L >> 4) & 0x0F0F0F0Fu) | (H & 0xF0F0F0F0u);
+        wl[j] = (L & 0x0F0F0F0Fu) | ((H & 0x0F0F0F0Fu) << 4);
+      }
+      if (valid) {
+        uint4* m4 = reinterpret_cast<uint4*>(p.k_msb + orow * (Dh / 2) + pp);
+        uint4* l4 = reinterpret_cast<uint4*>(p.k_lsb + orow * (Dh / 2) + pp);
+        m4[0] = make_uint4(wm[0], wm[1], wm[2], wm[3]);
+        m4[1] = make_uint4(wm[4], wm[5], wm[6], wm[7]);
+        l4[0] = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+        l4[1] = make_uint4(wl[4], wl[5], wl[6], wl[7]);
+      }
     }
-    if (valid) {
-      uint4* m4 = reinterpret_cast<uint4*>(p.k_msb + orow * (Dh / 2) + pp);
-      uint4* l4 = reinterpret_cast<uint4*>(p.k_lsb + orow * (Dh / 2) + pp);
-      m4[0] = make_uint4(wm[0], wm[1], wm[2], wm[3]);
-      m4[1] = make_uint4(wm[4], wm[5], wm[6], wm[7]);
-      l4[0] = make_uint4(wl[0], wl[1], wl[2], wl[3]);
-      l4[1] = make_uint4(wl[4], wl[5], wl[6], wl[7]);
-    }
-    if (valid && half == hc) p.k_scale[orow] = sc;
+    if (valid) p.k_scale[orow] = sc;
   }
 }
 
@@ -269,12 +263,12 @@ __global__ void __launch_bounds__(kThreads, 1) qkv_proj_kernel(const __grid_cons
       bool ok = true;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
         const Tile tile = tile_of(t, mt, tiles_per);
-        int wrow[2];
+        int wrow[PN / 64];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
+        for (int u = 0; u < PN / 64; ++u) {
           const int c = tile.col0 + 64 * u;
           int hs = c / p.Dh, off = c % p.Dh;
-          if (hs >= p.cur) {  // padding half of the last tile: any valid rows
+          if (hs >= p.cur) {  // padding of the last tile: any valid rows
             hs = p.cur - 1;
             off = 0;
           }
@@ -286,8 +280,9 @@ __global__ void __launch_bounds__(kThreads, 1) qkv_proj_kernel(const __grid_cons
           uint8_t* st = sm + L::oStage + s * L::kStageBytes;
           mbar_arrive_expect_tx(&full[s], L::kStageBytes);
           tma_load_2d(st, &P.tm_x, kb * PK, tile.m0, &full[s]);
-          tma_load_2d(st + L::kABytes, &P.tm_w, kb * PK, wrow[0], &full[s]);
-          tma_load_2d(st + L::kABytes + 64 * 128, &P.tm_w, kb * PK, wrow[1], &full[s]);
+#pragma unroll
+          for (int u = 0; u < PN / 64; ++u)
+            tma_load_2d(st + L::kABytes + u * 64 * 128, &P.tm_w, kb * PK, wrow[u], &full[s]);
         }
       }
       if (!ok) {  // let the copies in flight land before the CTA exits
@@ -330,6 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1) qkv_proj_kernel(const __grid_cons
     }
   } else {
     const int e = warp - 2, half = e >> 2, qd = warp & 3;
+    const int hpt = PN / p.Dh;  // heads per tile: warp half h takes heads [h * hpt / 2, (h + 1) * hpt / 2)
     const int r = qd * 32 + lane;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     int lt = 0;
@@ -339,8 +335,10 @@ __global__ void __launch_bounds__(kThreads, 1) qkv_proj_kernel(const __grid_cons
       ok = __all_sync(0xffffffffu, ok && !*abort);
       if (!ok) break;
       tc_fence_after();
-      epilogue_tile<T>(p, tmem + lane_base + buf * PN, tile_of(t, mt, tiles_per), r, half, T_,
-                       reinterpret_cast<float*>(sm + L::oBias) + e * 128);
+      const Tile tile = tile_of(t, mt, tiles_per);
+      for (int hc = half * hpt / 2; hc < (half + 1) * hpt / 2; ++hc)
+        epilogue_head<T>(p, tmem + lane_base + buf * PN, tile, r, hc, T_,
+                         reinterpret_cast<float*>(sm + L::oBias) + e * 128);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
