@@ -66,6 +66,8 @@ def parse():
                     help="run only the Qwen3 decode attention (--steps timed steps) and print its line")
     ap.add_argument("--decode-batch", type=int, default=64,
                     help="batch of the Qwen3 decode measurement (64; smaller for profiling captures)")
+    ap.add_argument("--only-bert", action="store_true",
+                    help="run only the BERT-base fp16 B32 S512 forward (one GPU) and print its line")
     ap.add_argument("--only-qwen3", action="store_true",
                     help="run only the Qwen3 prefill (--steps timed prefills) and print its line")
     return ap.parse_args()
@@ -750,6 +752,14 @@ def main():
             if world > 1:
                 import torch.distributed as dist
                 dist.destroy_process_group()
+        return
+    if args.only_bert:
+        if rank == 0:
+            dev = torch.device("cuda", local_rank)
+            torch.cuda.set_device(dev)
+            r = bert_bench(torch, 0, 1, dev, steps=args.steps)
+            print(json.dumps(dict(metric="bert_ms_per_batch", value=r["ms_per_batch"], unit="ms",
+                                  higher_is_better=False, n_gpus=1, **r)), flush=True)
         return
     if args.only_qwen3:
         if rank == 0:

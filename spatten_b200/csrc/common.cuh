@@ -114,6 +114,17 @@ SPATTEN_DEV float fast_exp2(float x) {
   return y;
 }
 
+// x / sc rounded to the nearest integer (ties to even), bit for bit what
+// rint(__fdiv_rn(x, sc)) gives, for |x| <= 127 * sc: x * (1 / sc) is within
+// 2 ulp of x / sc, so its rounding can only differ when it lies within a few
+// ulp of a half-integer; those rare values take the exact division.
+SPATTEN_DEV int quant_div(float x, float sc, float rc) {
+  const float y = x * rc;
+  const float t = rintf(y);
+  if (!(fabsf(y - t) <= 0.49990f)) return __float2int_rn(__fdiv_rn(x, sc));  // also NaN / inf (denormal sc)
+  return (int)t;
+}
+
 // Order-preserving map float -> uint32 (larger float -> larger key).
 SPATTEN_DEV uint32_t float_order_key(float f) {
   uint32_t u = __float_as_uint(f);

@@ -96,17 +96,6 @@ SPATTEN_DEV int head_of(const ProjParams& p, int hs) {
   return (h >= 0 && h < p.Hall) ? h : 0;
 }
 
-// x / sc rounded to the nearest integer (ties to even), bit for bit what
-// rint(__fdiv_rn(x, sc)) gives, for |x| <= 127 * sc: x * (1 / sc) is within
-// 2 ulp of x / sc, so its rounding can only differ when it lies within a few
-// ulp of a half-integer; those rare values take the exact division.
-SPATTEN_DEV int quant_div(float x, float sc, float rc) {
-  const float y = x * rc;
-  const float t = rintf(y);
-  if (fabsf(y - t) > 0.49990f) return __float2int_rn(__fdiv_rn(x, sc));
-  return (int)t;
-}
-
 // Epilogue of one head of a tile for one token row (TMEM lane r; `tl` is
 // the accumulator's lane base): head hc of the tile, all Dh of its columns.
 // Values are the rounded activations acc + bias; `sb` is this warp's

@@ -3,6 +3,7 @@
 // Replaces the reference's float split of K (k_msb = 0.8*K, k_lsb = 0.2*K,
 // spatten_bert_ultimate.py:184-185) with an integer one:
 //   scale = max|x| / 127, x8 = clamp(rint(x / scale), -127, 127)
+// (x / scale correctly rounded, as IEEE division gives it: quant_div)
 //   msb = x8 >> 4 (signed nibble), lsb = x8 & 15, x8 == 16*msb + lsb.
 // Packing: byte p of a row holds dim p (low nibble) and dim p + D/2 (high).
 //
@@ -48,12 +49,13 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float s = __fdiv_rn(amax, 127.0f);
+    const float rs = s != 0.f ? 1.0f / s : 0.f;
     int qv[E];
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       int t = 0;
       if (s != 0.f) {
-        t = __float2int_rn(__fdiv_rn(v[e], s));
+        t = quant_div(v[e], s, rs);
         t = max(-127, min(127, t));
       }
       qv[e] = t;
@@ -125,6 +127,7 @@ __global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict
 #pragma unroll
     for (int o = LPR / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float s = __fdiv_rn(amax, 127.0f);
+    const float rs = s != 0.f ? 1.0f / s : 0.f;
     uint32_t w[NWORD];
 #pragma unroll
     for (int k = 0; k < NWORD; ++k) {
@@ -133,7 +136,7 @@ __global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict
       for (int b = 0; b < 4; ++b) {
         int t = 0;
         if (s != 0.f) {
-          t = __float2int_rn(__fdiv_rn(v[4 * k + b], s));
+          t = quant_div(v[4 * k + b], s, rs);
           t = max(-127, min(127, t));
         }
         packed |= ((uint32_t)t & 0xFFu) << (8 * b);
