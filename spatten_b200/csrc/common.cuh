@@ -125,6 +125,28 @@ SPATTEN_DEV int quant_div(float x, float sc, float rc) {
   return (int)t;
 }
 
+// a / 127 rounded to nearest even (the quantisation scale max|x| / 127), for
+// finite a >= 0, by Markstein's correction step (P. Markstein, "Computation
+// of elementary functions on the IBM RISC System/6000 processor", 1990):
+// with y = RN(1/127) and q = RN(a * y), the remainder a - 127 q is exact in
+// one FMA and RN(q + remainder * y) is the correctly rounded quotient.
+// Below 2^-100 (where q could be subnormal) the IEEE division is used.
+SPATTEN_DEV float div127_rn(float a) {
+  if (a < 7.8886091e-31f) return __fdiv_rn(a, 127.0f);
+  constexpr float y = 1.0f / 127.0f;
+  const float q = a * y;
+  const float r = fmaf(-q, 127.0f, a);
+  return fmaf(r, y, q);
+}
+
+// 1 / s to within an ulp (ex2-style approximation instruction); quant_div
+// only needs its product with x within ~1e-4 of x / s.
+SPATTEN_DEV float rcp_approx(float s) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
+  return r;
+}
+
 // Order-preserving map float -> uint32 (larger float -> larger key).
 SPATTEN_DEV uint32_t float_order_key(float f) {
   uint32_t u = __float_as_uint(f);

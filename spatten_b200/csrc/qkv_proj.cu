@@ -145,17 +145,29 @@ SPATTEN_DEV void epilogue_head(const ProjParams& p, uint32_t tl, const Tile& tl_
 #pragma unroll
     for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(round_to<T>(__uint_as_float(a[i]) + sb[cc + i])));
   }
-  const float sc = __fdiv_rn(amax, 127.0f);
-  const float rc = sc != 0.f ? 1.0f / sc : 0.f;
-  // four int8 of head columns c .. c+3 (a[i] .. a[i+3]), packed little-endian
+  const float sc = div127_rn(amax);
+  const float rc = rcp_approx(sc);
+  // four int8 of head columns c .. c+3 (a[i] .. a[i+3]), packed little-endian:
+  // x * (1 / sc), and the exact division (quant_div) only when one of the
+  // four lands within 1e-4 of a rounding tie
   auto q4 = [&](const uint32_t (&a)[32], int i, int c) -> uint32_t {
-    uint32_t w = 0;
+    if (sc == 0.f) return 0u;
+    float x[4];
+    int t[4];
+    bool near_tie = false;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int t = sc != 0.f ? quant_div(round_to<T>(__uint_as_float(a[i + e]) + sb[c + e]), sc, rc) : 0;
-      w |= ((uint32_t)t & 0xFFu) << (8 * e);
+      x[e] = round_to<T>(__uint_as_float(a[i + e]) + sb[c + e]);
+      const float y = x[e] * rc, ti = rintf(y);
+      near_tie |= !(fabsf(y - ti) <= 0.49990f);
+      t[e] = (int)ti;
     }
-    return w;
+    if (near_tie) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) t[e] = quant_div(x[e], sc, rc);
+    }
+    return ((uint32_t)t[0] & 0xFFu) | (((uint32_t)t[1] & 0xFFu) << 8) | (((uint32_t)t[2] & 0xFFu) << 16) |
+           ((uint32_t)t[3] << 24);
   };
   if (tl_.which == 0) {
     int8_t* dst = p.q8 + orow * Dh;

@@ -18,6 +18,22 @@
 
 namespace spatten {
 
+// (z, h, m) of row r of a [Z, H, M] grid of rows; 32-bit divisions when the
+// row count allows (a 64-bit division is a long instruction sequence).
+SPATTEN_DEV void row_coords(int64_t r, int M, int H, int64_t& m, int64_t& h, int64_t& z) {
+  if (r < 0x7FFFFFFF) {
+    const uint32_t ru = (uint32_t)r, zh = ru / (uint32_t)M;
+    m = ru - zh * (uint32_t)M;
+    z = zh / (uint32_t)H;
+    h = zh - (uint32_t)z * (uint32_t)H;
+  } else {
+    m = r % M;
+    const int64_t zh = r / M;
+    h = zh % H;
+    z = zh / H;
+  }
+}
+
 template <typename T, int E>
 SPATTEN_DEV void load_row(const T* p, float (&v)[E]) {
 #pragma unroll
@@ -37,9 +53,8 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
        r += warps) {
-    const int64_t m = r % M;
-    const int64_t zh = r / M;
-    const int64_t h = zh % H, z = zh / H;
+    int64_t m, h, z;
+    row_coords(r, M, H, m, h, z);
     const T* src = x + z * sz + h * sh + m * sm + lane * E;
     float v[E];
     load_row<T, E>(src, v);
@@ -111,8 +126,8 @@ __global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict
     const bool live = r < rows;
     float v[EPL];
     if (live) {
-      const int64_t m = r % M, zh = r / M;
-      const int64_t h = zh % H, z = zh / H;
+      int64_t m, h, z;
+      row_coords(r, M, H, m, h, z);
       const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + z * sz + h * sh + m * sm) + li);
       const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
@@ -126,23 +141,33 @@ __global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict
     for (int i = 0; i < EPL; ++i) amax = fmaxf(amax, fabsf(v[i]));
 #pragma unroll
     for (int o = LPR / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float s = __fdiv_rn(amax, 127.0f);
-    const float rs = s != 0.f ? 1.0f / s : 0.f;
+    const float s = div127_rn(amax);
+    const float rs = rcp_approx(s);
+    // |x| <= amax and s = RN(amax / 127) keep |x / s| <= 127 * (1 + 2^-23):
+    // the rounded quotient never leaves [-127, 127], no clamp needed
+    // x / s as x * (1 / s); the exact division only for the lane's values
+    // that land within 1e-4 of a rounding tie (quant_div's rule), decided
+    // once per lane so that the common path has no branch per value
+    int t[EPL];
+    bool near_tie = false;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const float y = v[i] * rs, ti = rintf(y);
+      near_tie |= !(fabsf(y - ti) <= 0.49990f);
+      t[i] = (int)ti;
+    }
+    if (s == 0.f) {
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) t[i] = 0;
+    } else if (near_tie) {
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) t[i] = quant_div(v[i], s, rs);
+    }
     uint32_t w[NWORD];
 #pragma unroll
-    for (int k = 0; k < NWORD; ++k) {
-      uint32_t packed = 0;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        int t = 0;
-        if (s != 0.f) {
-          t = quant_div(v[4 * k + b], s, rs);
-          t = max(-127, min(127, t));
-        }
-        packed |= ((uint32_t)t & 0xFFu) << (8 * b);
-      }
-      w[k] = packed;
-    }
+    for (int k = 0; k < NWORD; ++k)
+      w[k] = ((uint32_t)t[4 * k] & 0xFFu) | (((uint32_t)t[4 * k + 1] & 0xFFu) << 8) |
+             (((uint32_t)t[4 * k + 2] & 0xFFu) << 16) | ((uint32_t)t[4 * k + 3] << 24);
     if (live && li == 0) scale[r] = s;
     if (!PLANES) {
       if (live) {
