@@ -101,10 +101,10 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
 }
 
 // Vector variant for rows whose start is 16-byte aligned (every row when the
-// base and the strides are): LPR = D / (16 / sizeof(T)) lanes per row, each
-// with one 16-byte load of EPL consecutive elements, 32 / LPR rows per warp
+// base and the strides are): LPR = D / (32 / sizeof(T)) lanes per row, each
+// with two 16-byte loads of EPL consecutive elements, 32 / LPR rows per warp
 // step; the row max is a reduction over the row's lanes, and the quantised
-// bytes leave in one 4- or 8-byte store per lane. Same arithmetic as above.
+// bytes leave in one 8- or 16-byte store per lane. Same arithmetic as above.
 template <typename T, int D, bool PLANES>
 __global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict__ x, int Z, int H,
                                                              int M, int64_t sz, int64_t sh,
@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict
                                                              uint8_t* __restrict__ msb,
                                                              uint8_t* __restrict__ lsb,
                                                              float* __restrict__ scale) {
-  constexpr int EPL = 16 / sizeof(T);  // elements per lane
+  constexpr int EPL = 32 / sizeof(T);  // elements per lane: two 16-byte loads
   constexpr int LPR = D / EPL;         // lanes per row
   constexpr int RPW = 32 / LPR;        // rows per warp step
   constexpr int NWORD = EPL / 4;       // packed int8 words per lane
@@ -128,8 +128,9 @@ __global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict
     if (live) {
       int64_t m, h, z;
       row_coords(r, M, H, m, h, z);
-      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + z * sz + h * sh + m * sm) + li);
-      const T* e = reinterpret_cast<const T*>(&raw);
+      const uint4* src = reinterpret_cast<const uint4*>(x + z * sz + h * sh + m * sm) + 2 * li;
+      const uint4 raw[2] = {__ldg(src), __ldg(src + 1)};
+      const T* e = reinterpret_cast<const T*>(raw);
 #pragma unroll
       for (int i = 0; i < EPL; ++i) v[i] = to_f32<T>(e[i]);
     } else {
@@ -172,8 +173,8 @@ __global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict
     if (!PLANES) {
       if (live) {
         int8_t* dst = q8 + r * D + li * EPL;
-        if constexpr (NWORD == 2) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
-        else *reinterpret_cast<uint32_t*>(dst) = w[0];
+        if constexpr (NWORD == 4) *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        else *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
       }
     } else {
       // lane li < LPR/2 holds dims [li*EPL, +EPL) = the low nibbles of those
@@ -190,12 +191,12 @@ __global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict
         }
         uint8_t* dm = msb + r * (D / 2) + li * EPL;
         uint8_t* dl = lsb + r * (D / 2) + li * EPL;
-        if constexpr (NWORD == 2) {
+        if constexpr (NWORD == 4) {
+          *reinterpret_cast<uint4*>(dm) = make_uint4(pm[0], pm[1], pm[2], pm[3]);
+          *reinterpret_cast<uint4*>(dl) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+        } else {
           *reinterpret_cast<uint2*>(dm) = make_uint2(pm[0], pm[1]);
           *reinterpret_cast<uint2*>(dl) = make_uint2(pl[0], pl[1]);
-        } else {
-          *reinterpret_cast<uint32_t*>(dm) = pm[0];
-          *reinterpret_cast<uint32_t*>(dl) = pl[0];
         }
       }
     }
@@ -206,7 +207,7 @@ template <typename T, int D, bool PLANES>
 static cudaError_t launch_quant_vec(const T* x, int Z, int H, int M, int64_t sz, int64_t sh, int64_t sm,
                                     int8_t* q8, uint8_t* msb, uint8_t* lsb, float* scale, cudaStream_t st,
                                     int64_t blocks) {
-  constexpr int LPR = D / (16 / (int)sizeof(T));
+  constexpr int LPR = D / (32 / (int)sizeof(T));
   if constexpr (LPR >= 2 && LPR <= 32) {
     quant_rows_vec_kernel<T, D, PLANES><<<(unsigned)blocks, 256, 0, st>>>(x, Z, H, M, sz, sh, sm, q8, msb,
                                                                           lsb, scale);
@@ -229,7 +230,7 @@ static cudaError_t launch_quant_t(const void* x, int Z, int H, int M, int D, int
   const T* xp = static_cast<const T*>(x);
   const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (sz * (int64_t)sizeof(T)) % 16 == 0 &&
                    (sh * (int64_t)sizeof(T)) % 16 == 0 && (sm * (int64_t)sizeof(T)) % 16 == 0;
-  constexpr int EPL = 16 / sizeof(T);
+  constexpr int EPL = 32 / sizeof(T);  // elements per lane of the vector kernel
   if (vec && D >= 2 * EPL && D <= 32 * EPL) {
     const int rpw = 32 / (D / EPL);
     int64_t vblocks = (rows + 8 * rpw - 1) / (8 * rpw);
