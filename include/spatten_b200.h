@@ -262,6 +262,47 @@ typedef struct {
 int spatten_qkv_proj(const spatten_qkv_proj_args* a, void* stream);
 
 /*
+ * Per-head RMSNorm (QK-norm) + rotary position embedding of the query and key
+ * projections, the query quantised to int8. No reference code (the reference
+ * has no Qwen3 path): replaces, inside the Qwen3 drop-in, the HF modules'
+ * q_norm / k_norm (Qwen3RMSNorm) and apply_rotary_pos_emb
+ * (transformers/models/qwen3/modeling_qwen3.py) and the query's
+ * spatten_quant_q_int8, with the HF arithmetic step for step: for each head
+ * row x, y = T(x * rsqrtf(mean(x^2) + eps)), n = T(w * y),
+ * out = T(T(n * cos) + T(rotate_half(n) * sin)) (T: rounding to dtype; the
+ * sum of squares is taken in this kernel's own order), then Q's int8 rows
+ * as spatten_quant_q_int8 computes them.
+ * q [B*S, >= Hq*D], k [B*S, >= Hk*D] (row t = b*S + s, row strides in
+ * elements); q_norm_w, k_norm_w [D]; cos, sin [B, S, D] (element strides
+ * cs_b_stride, cs_s_stride). Outputs: k_out [B*S, Hk*D] rows (token-major,
+ * like the HF key states); q_out (same layout, optional) and / or q8
+ * [B, Hq, S, D] int8 + q_scale [B, Hq, S]. D in {64, 128}; dtype f16 / bf16;
+ * pointers 16-byte aligned, strides multiples of 8 elements.
+ */
+typedef struct {
+  int dtype;
+  int B, S, Hq, Hk, D;
+  const void* q;
+  int64_t q_row_stride;
+  const void* k;
+  int64_t k_row_stride;
+  const void* q_norm_w;
+  const void* k_norm_w;
+  float eps;
+  const void* cos;
+  const void* sin;
+  int64_t cs_b_stride, cs_s_stride;
+  void* k_out;
+  int64_t k_out_row_stride;
+  void* q_out;
+  int64_t q_out_row_stride;
+  int8_t* q8;
+  float* q_scale;
+} spatten_qk_norm_rope_args;
+
+int spatten_qk_norm_rope(const spatten_qk_norm_rope_args* a, void* stream);
+
+/*
  * Top-k selection, indices returned in ascending order:
  *   out[r, :] = sort(topk(x[r, :n], k).indices), r < rows
  * Ties at the k-th value go to the smaller index. x fp32 with row stride

@@ -69,6 +69,17 @@ class QkvProjArgs(ctypes.Structure):
     ]
 
 
+class QkNormRopeArgs(ctypes.Structure):
+    """Mirror of spatten_qk_norm_rope_args (include/spatten_b200.h)."""
+    _fields_ = [
+        ("dtype", c_int), ("B", c_int), ("S", c_int), ("Hq", c_int), ("Hk", c_int), ("D", c_int),
+        ("q", c_vp), ("q_row_stride", c_i64), ("k", c_vp), ("k_row_stride", c_i64),
+        ("q_norm_w", c_vp), ("k_norm_w", c_vp), ("eps", c_float), ("cos", c_vp), ("sin", c_vp),
+        ("cs_b_stride", c_i64), ("cs_s_stride", c_i64), ("k_out", c_vp), ("k_out_row_stride", c_i64),
+        ("q_out", c_vp), ("q_out_row_stride", c_i64), ("q8", c_vp), ("q_scale", c_vp),
+    ]
+
+
 # name -> (restype, argtypes); every entry point declared in include/spatten_b200.h
 SIGNATURES = {
     "spatten_abi_version": (c_int, []),
@@ -87,6 +98,7 @@ SIGNATURES = {
     "spatten_decode_importance": (c_int, [ctypes.POINTER(DecodeArgs), c_vp, ctypes.c_size_t, c_vp]),
     "spatten_decode_attend": (c_int, [ctypes.POINTER(DecodeArgs), c_vp, ctypes.c_size_t, c_vp]),
     "spatten_qkv_proj": (c_int, [ctypes.POINTER(QkvProjArgs), c_vp]),
+    "spatten_qk_norm_rope": (c_int, [ctypes.POINTER(QkNormRopeArgs), c_vp]),
     "spatten_gather_rows": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_int, c_int, c_int,
                                     c_i64, c_i64, c_vp, c_i64, c_i64, c_vp]),
 }

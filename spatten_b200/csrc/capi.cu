@@ -392,4 +392,42 @@ int spatten_qkv_proj(const spatten_qkv_proj_args* a, void* stream) {
   return cuda_status(spatten::launch_qkv_proj(p, (cudaStream_t)stream), "qkv_proj launch");
 }
 
+int spatten_qk_norm_rope(const spatten_qk_norm_rope_args* a, void* stream) {
+  if (!a) return fail(SPATTEN_ERR_INVALID, "qk_norm_rope: null args");
+  if (a->dtype != SPATTEN_DTYPE_F16 && a->dtype != SPATTEN_DTYPE_BF16)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "qk_norm_rope: dtype %d (need f16 or bf16)", a->dtype);
+  if (a->D != 64 && a->D != 128) return fail(SPATTEN_ERR_UNSUPPORTED, "qk_norm_rope: D=%d (need 64 or 128)", a->D);
+  if (a->B < 1 || a->S < 1 || a->Hq < 1 || a->Hk < 1)
+    return fail(SPATTEN_ERR_INVALID, "qk_norm_rope: empty shape B=%d S=%d Hq=%d Hk=%d", a->B, a->S, a->Hq, a->Hk);
+  if ((int64_t)a->B * a->S > ((int64_t)1 << 31) - 1)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "qk_norm_rope: too many tokens");
+  if (!a->q || !a->k || !a->q_norm_w || !a->k_norm_w || !a->cos || !a->sin || !a->k_out)
+    return fail(SPATTEN_ERR_INVALID, "qk_norm_rope: null input or k_out");
+  if (!a->q_out && !a->q8) return fail(SPATTEN_ERR_INVALID, "qk_norm_rope: neither q_out nor q8 given");
+  if (a->q8 && !a->q_scale) return fail(SPATTEN_ERR_INVALID, "qk_norm_rope: q8 without q_scale");
+  if (a->q_row_stride < (int64_t)a->Hq * a->D || a->k_row_stride < (int64_t)a->Hk * a->D ||
+      a->k_out_row_stride < (int64_t)a->Hk * a->D || (a->q_out && a->q_out_row_stride < (int64_t)a->Hq * a->D))
+    return fail(SPATTEN_ERR_INVALID, "qk_norm_rope: row stride shorter than the heads");
+  if (a->cs_b_stride < 0 || a->cs_s_stride < a->D)
+    return fail(SPATTEN_ERR_INVALID, "qk_norm_rope: bad cos/sin strides");
+  const void* ptrs16[] = {a->q, a->k, a->q_norm_w, a->k_norm_w, a->cos, a->sin, a->k_out, a->q_out, a->q8};
+  for (const void* ptr : ptrs16)
+    if (ptr && !aligned(ptr, 16)) return fail(SPATTEN_ERR_INVALID, "qk_norm_rope: a pointer is not 16-byte aligned");
+  const int64_t strides[] = {a->q_row_stride, a->k_row_stride, a->k_out_row_stride,
+                             a->q_out ? a->q_out_row_stride : 0, a->cs_b_stride, a->cs_s_stride};
+  for (int64_t s : strides)
+    if (s % 8) return fail(SPATTEN_ERR_INVALID, "qk_norm_rope: strides must be multiples of 8 elements");
+  if (a->q_scale && !aligned(a->q_scale, 4)) return fail(SPATTEN_ERR_INVALID, "qk_norm_rope: q_scale misaligned");
+  spatten::QkPrepParams p;
+  p.dtype = a->dtype;
+  p.B = a->B; p.S = a->S; p.Hq = a->Hq; p.Hk = a->Hk; p.D = a->D;
+  p.q = a->q; p.q_st = a->q_row_stride; p.k = a->k; p.k_st = a->k_row_stride;
+  p.q_w = a->q_norm_w; p.k_w = a->k_norm_w; p.eps = a->eps;
+  p.cos = a->cos; p.sin = a->sin; p.cs_sb = a->cs_b_stride; p.cs_ss = a->cs_s_stride;
+  p.k_out = a->k_out; p.ko_st = a->k_out_row_stride;
+  p.q_out = a->q_out; p.qo_st = a->q_out_row_stride;
+  p.q8 = a->q8; p.q_scale = a->q_scale;
+  return cuda_status(spatten::launch_qk_prep(p, (cudaStream_t)stream), "qk_norm_rope launch");
+}
+
 }  // extern "C"

@@ -75,4 +75,27 @@ cudaError_t launch_gather(const void* src, int64_t src_b, int64_t src_r, const i
                           int64_t row_bytes, void* dst, int64_t dst_b, int64_t dst_r,
                           cudaStream_t st, int n_sm, int64_t src_rows);
 
+// Per-head RMSNorm + rotary embedding of Q and K, Q quantised (qk_prep.cu).
+struct QkPrepParams {
+  int dtype;                 // kF16 / kBF16: projections, weights, cos / sin, outputs
+  int B, S, Hq, Hk, D;       // tokens t = b * S + s
+  const void* q;             // [T, >= Hq * D] rows, row stride q_st elements
+  int64_t q_st;
+  const void* k;             // [T, >= Hk * D] rows, row stride k_st
+  int64_t k_st;
+  const void* q_w;           // [D] query norm weight
+  const void* k_w;           // [D] key norm weight
+  float eps;
+  const void* cos;           // [B, S, D] element strides cs_sb, cs_ss (last dim contiguous)
+  const void* sin;
+  int64_t cs_sb, cs_ss;
+  void* k_out;               // [T, Hk * D] rows, stride ko_st
+  int64_t ko_st;
+  void* q_out;               // [T, Hq * D] rows, stride qo_st, or null
+  int64_t qo_st;
+  int8_t* q8;                // [B, Hq, S, D] or null
+  float* q_scale;            // [B, Hq, S]
+};
+cudaError_t launch_qk_prep(const QkPrepParams& p, cudaStream_t st);
+
 }  // namespace spatten

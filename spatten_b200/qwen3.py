@@ -1,8 +1,10 @@
 """Drop-in SpAtten cascade for Hugging Face Qwen3 prefill, on the C-ABI kernels.
 
 ``SpattenQwen3Attention(config, layer_idx)`` subclasses HF ``Qwen3Attention``
-(installed ``transformers/models/qwen3/modeling_qwen3.py``: projections,
-per-head RMSNorm QK-norm and RoPE are the HF module's own) and replaces its
+(installed ``transformers/models/qwen3/modeling_qwen3.py``: the projections
+are the HF module's own; for fp16 / bf16 its per-head RMSNorm QK-norm and
+RoPE run as one kernel, ``qk_norm_rope``, with the HF arithmetic and the
+query's int8 quantisation; fp32 keeps the HF modules) and replaces its
 attention core with the progressive sparse attention kernel:
 
 * GQA: Q heads share KV heads as in HF's ``repeat_kv`` (head h reads KV head
@@ -43,6 +45,51 @@ from .select import gather_rows, topk_indices
 def keep_count(ratio, current):
     """``max(1, ceil(ratio * current))``, exact on the ratio's decimal repr."""
     return max(1, math.ceil(Fraction(repr(float(ratio))) * current))
+
+
+_DT = {torch.float16: N.DTYPE_F16, torch.bfloat16: N.DTYPE_BF16}
+
+
+def qk_norm_rope(q, k, q_norm, k_norm, cos, sin, Hq, Hk, D, quantize_q):
+    """QK-norm + RoPE of the projections in one kernel (spatten_qk_norm_rope):
+    q [B, S, Hq*D], k [B, S, Hk*D] (fp16 / bf16, rows contiguous), the HF
+    Qwen3RMSNorm modules ``q_norm`` / ``k_norm``, cos / sin [B, S, D].
+    Returns (q [B, S, Hq, D] or None, q8 [B, Hq, S, D] or None, q_scale
+    [B, Hq, S] or None, k [B, S, Hk, D]); q8 / q_scale when ``quantize_q``,
+    q otherwise."""
+    B, S, _ = q.shape
+    if q.stride(2) != 1 or q.stride(0) != S * q.stride(1):
+        q = q.contiguous()
+    if k.stride(2) != 1 or k.stride(0) != S * k.stride(1):
+        k = k.contiguous()
+    if cos.stride(-1) != 1 or sin.stride() != cos.stride():
+        cos, sin = cos.contiguous(), sin.contiguous()
+    wq, wk = q_norm.weight.contiguous(), k_norm.weight.contiguous()
+    dev, dt = q.device, q.dtype
+    a = N.QkNormRopeArgs()
+    a.dtype = _DT[dt]
+    a.B, a.S, a.Hq, a.Hk, a.D = B, S, Hq, Hk, D
+    a.q, a.q_row_stride = q.data_ptr(), q.stride(1)
+    a.k, a.k_row_stride = k.data_ptr(), k.stride(1)
+    a.q_norm_w, a.k_norm_w = wq.data_ptr(), wk.data_ptr()
+    if float(k_norm.variance_epsilon) != float(q_norm.variance_epsilon):
+        raise ValueError("qk_norm_rope: q_norm and k_norm must share their epsilon")
+    a.eps = float(q_norm.variance_epsilon)
+    a.cos, a.sin = cos.data_ptr(), sin.data_ptr()
+    a.cs_b_stride = cos.stride(0) if cos.shape[0] == B else 0
+    a.cs_s_stride = cos.stride(1)
+    k_out = torch.empty((B, S, Hk, D), dtype=dt, device=dev)
+    a.k_out, a.k_out_row_stride = k_out.data_ptr(), Hk * D
+    q_out = q8 = qs = None
+    if quantize_q:
+        q8 = torch.empty((B, Hq, S, D), dtype=torch.int8, device=dev)
+        qs = torch.empty((B, Hq, S), dtype=torch.float32, device=dev)
+        a.q8, a.q_scale = q8.data_ptr(), qs.data_ptr()
+    else:
+        q_out = torch.empty((B, S, Hq, D), dtype=dt, device=dev)
+        a.q_out, a.q_out_row_stride = q_out.data_ptr(), Hq * D
+    N.check(N.lib.spatten_qk_norm_rope(a, torch.cuda.current_stream(dev).cuda_stream))
+    return q_out, q8, qs, k_out
 
 
 class CascadeState:
@@ -98,11 +145,18 @@ class SpattenQwen3Attention(Qwen3Attention):
             raise NotImplementedError("SpattenQwen3Attention: prefill only (the cache already holds keys)")
         H, Hkv, d = self.num_heads, self.num_kv_heads, self.head_dim
         dev = hidden_states.device
-        q = self.q_norm(self.q_proj(hidden_states).view(B, S, H, d))
-        k = self.k_norm(self.k_proj(hidden_states).view(B, S, Hkv, d))
-        v = self.v_proj(hidden_states).view(B, S, Hkv, d)
         cos, sin = position_embeddings
-        q, k = apply_rotary_pos_emb(q, k, cos, sin, unsqueeze_dim=2)
+        q8 = qs = None
+        if hidden_states.dtype in _DT and d in (64, 128):
+            # QK-norm + RoPE (+ the query's int8) in one kernel: the HF
+            # arithmetic without its dozen elementwise launches
+            q, q8, qs, k = qk_norm_rope(self.q_proj(hidden_states), self.k_proj(hidden_states), self.q_norm,
+                                        self.k_norm, cos, sin, H, Hkv, d, self.enable_prog_quant)
+        else:
+            q = self.q_norm(self.q_proj(hidden_states).view(B, S, H, d))
+            k = self.k_norm(self.k_proj(hidden_states).view(B, S, Hkv, d))
+            q, k = apply_rotary_pos_emb(q, k, cos, sin, unsqueeze_dim=2)
+        v = self.v_proj(hidden_states).view(B, S, Hkv, d)
 
         st = self.cascade
         if self.layer_idx == 0 or st.positions is None or st.positions.shape[0] != B:
@@ -123,13 +177,14 @@ class SpattenQwen3Attention(Qwen3Attention):
 
         out = torch.empty(B, S, H, d, dtype=hidden_states.dtype, device=dev)
         v_thr, v_count = self._v_prune(K)
-        qh = q.permute(0, 2, 1, 3)   # [B, H, S, d] views
+        qh = q.permute(0, 2, 1, 3) if q is not None else None  # [B, H, S, d] views
         kh = k.permute(0, 2, 1, 3)   # [B, Hkv, K, d]
         vh = v.permute(0, 2, 1, 3)
         common = dict(sm_scale=self.scaling, v_thr=v_thr, v_prune_count=v_count, key_limit=key_limit,
                       tok_in=st.cumulative, want_tok=True, out=out.permute(0, 2, 1, 3))
         if self.enable_prog_quant:
-            q8, qs = quant_q_int8(qh)
+            if q8 is None:
+                q8, qs = quant_q_int8(qh)
             kp = quant_k_planes(kh)
             r = prog_attn(q8, kp.msb, vh, k1=kp.lsb, mode=N.MODE_QUANT, q_scale=qs, k_scale=kp.scale,
                           refetch_thr=float(self.quant_threshold), want_refetch=True, **common)
@@ -142,7 +197,9 @@ class SpattenQwen3Attention(Qwen3Attention):
         st.kept_per_layer.append(K)
 
         if past_key_values is not None:
-            past_key_values.update(kh.contiguous(), vh.contiguous(), self.layer_idx)
+            # the cache concatenates into a new contiguous [B, Hkv, K, d] tensor
+            # itself: the head-major views go in as they are (one copy, not two)
+            past_key_values.update(kh, vh, self.layer_idx)
 
         if self.enable_token_prune:
             keep = keep_count(self.token_keep_ratio, K) if self.token_keep_ratio is not None \

@@ -191,3 +191,24 @@ def test_qkv_proj_args_validation():
     assert N.lib.spatten_qkv_proj(a, None) == N.ERR_INVALID
     a.x_row_stride, a.x = 768, (1 << 20) + 8  # x not 16-byte aligned
     assert N.lib.spatten_qkv_proj(a, None) == N.ERR_INVALID
+
+
+def test_qk_norm_rope_args_validation():
+    """The fused QK-norm + RoPE rejects bad arguments before any launch."""
+    from spatten_b200 import _native as N
+    assert N.lib.spatten_qk_norm_rope(None, None) == N.ERR_INVALID
+    a = N.QkNormRopeArgs()
+    a.dtype, a.B, a.S, a.Hq, a.Hk, a.D = N.DTYPE_BF16, 2, 100, 16, 8, 128
+    a.q = a.k = a.q_norm_w = a.k_norm_w = a.cos = a.sin = a.k_out = 1 << 20
+    a.q_row_stride, a.k_row_stride, a.k_out_row_stride = 2048, 1024, 1024
+    a.cs_b_stride, a.cs_s_stride, a.eps = 100 * 128, 128, 1e-6
+    assert N.lib.spatten_qk_norm_rope(a, None) == N.ERR_INVALID  # neither q_out nor q8
+    a.q8, a.q_scale = 1 << 21, 1 << 22
+    a.D = 96
+    assert N.lib.spatten_qk_norm_rope(a, None) == N.ERR_UNSUPPORTED
+    a.D, a.dtype = 128, N.DTYPE_F32
+    assert N.lib.spatten_qk_norm_rope(a, None) == N.ERR_UNSUPPORTED
+    a.dtype, a.q_row_stride = N.DTYPE_BF16, 1000  # shorter than Hq * D
+    assert N.lib.spatten_qk_norm_rope(a, None) == N.ERR_INVALID
+    a.q_row_stride, a.k = 2048, (1 << 20) + 4
+    assert N.lib.spatten_qk_norm_rope(a, None) == N.ERR_INVALID
