@@ -171,7 +171,10 @@ struct Cta {
     b.o_full = bar++;
     abort = reinterpret_cast<volatile int*>(sm + L::oFlag);
     decision = reinterpret_cast<int*>(sm + L::oFlag + 4);
-    mt = blockIdx.x;
+    // With a causal mask or key limits the work grows with the row index:
+    // the launch order runs each head's query tiles heaviest first, so the
+    // last CTAs to start are short ones and the tail stays short.
+    mt = (p.causal || p.key_limit) ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
     h = blockIdx.y;
     z = blockIdx.z;
     kvh = h / (p.H / p.Hkv);
