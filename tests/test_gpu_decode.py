@@ -30,6 +30,8 @@ def _case(B, H, G, N, D, dt, seed):
 @pytest.mark.parametrize("B,H,G,N,D,top_k,n_valid,dt", [
     (3, 8, 2, 3000, 128, 300, 2900, torch.float16),
     (2, 8, 1, 1500, 128, 257, None, torch.bfloat16),
+    # one KV head and its 4 query heads: a Qwen3-8B layer split over 8 ranks
+    (2, 4, 1, 4096, 128, 512, None, torch.bfloat16),
     (2, 4, 4, 700, 64, 100, 650, torch.float16),
     (1, 16, 2, 2048, 128, 2048, None, torch.bfloat16),
     (1, 32, 8, 16384, 128, 2048, 16000, torch.bfloat16),
