@@ -34,6 +34,10 @@
  *       slice_linear_weights (module.py:12-34) + the Q/K/V projections of
  *       SpattenBertSelfAttention.forward (spatten_bert.py:72-78) + the K
  *       plane split (spatten_bert_ultimate.py:184-185), in one kernel.
+ *   spatten_compact_out_proj
+ *       the next layer's hidden-state gather (module.py:49-54) moved into the
+ *       attention output projection + residual, so the FFN runs on the
+ *       compacted sequence.
  */
 #ifndef SPATTEN_B200_H
 #define SPATTEN_B200_H
@@ -301,6 +305,42 @@ typedef struct {
 } spatten_qk_norm_rope_args;
 
 int spatten_qk_norm_rope(const spatten_qk_norm_rope_args* a, void* stream);
+
+/*
+ * Attention output projection + residual of the kept tokens only (the token
+ * gather of the cascade folded into the GEMM's row loads). Replaces, for a
+ * layer whose attention chose the tokens the next layer keeps, the gather of
+ * the next layer's hidden states (module.py:49-54, torch.gather) moved ahead
+ * of the first row-wise step after the attention, HF BertSelfOutput's
+ * dense + residual add (transformers/models/bert/modeling_bert.py), so the
+ * LayerNorm and the FFN that follow run on the compacted sequence:
+ *   out[b*L + j, :] = T(T(ctx[b*S + s, :] . w^T + bias) + res[b*S + s, :]),
+ *   s = kept[b, j]
+ * (T: rounding to dtype). The dot product runs over the active heads'
+ * column blocks of the context row only (heads[cur], null = 0 .. cur-1; the
+ * other heads' blocks are zeros in the drop-in's context). ctx
+ * [B*S, >= H*head_dim] and res [B*S, >= N] with row strides in elements; w
+ * [N, H*head_dim] (nn.Linear layout) contiguous; bias [N] or null; kept
+ * int64 [B, L] (positions outside [0, S) are clamped); out [B*L, N]
+ * contiguous. dtype f16 / bf16; head_dim a multiple of 64; N a multiple of
+ * 32; pointers 16-byte aligned; strides multiples of 8 elements.
+ */
+typedef struct {
+  int dtype;
+  int B, S, L, N;
+  int H, head_dim, cur;
+  const int64_t* heads;
+  const int64_t* kept;
+  const void* ctx;
+  int64_t ctx_row_stride;
+  const void* w;
+  const void* bias;
+  const void* res;
+  int64_t res_row_stride;
+  void* out;
+} spatten_compact_out_proj_args;
+
+int spatten_compact_out_proj(const spatten_compact_out_proj_args* a, void* stream);
 
 /*
  * Top-k selection, indices returned in ascending order:

@@ -80,6 +80,16 @@ class QkNormRopeArgs(ctypes.Structure):
     ]
 
 
+class CompactOutProjArgs(ctypes.Structure):
+    """Mirror of spatten_compact_out_proj_args (include/spatten_b200.h)."""
+    _fields_ = [
+        ("dtype", c_int), ("B", c_int), ("S", c_int), ("L", c_int), ("N", c_int),
+        ("H", c_int), ("head_dim", c_int), ("cur", c_int), ("heads", c_vp), ("kept", c_vp),
+        ("ctx", c_vp), ("ctx_row_stride", c_i64), ("w", c_vp), ("bias", c_vp),
+        ("res", c_vp), ("res_row_stride", c_i64), ("out", c_vp),
+    ]
+
+
 # name -> (restype, argtypes); every entry point declared in include/spatten_b200.h
 SIGNATURES = {
     "spatten_abi_version": (c_int, []),
@@ -99,6 +109,7 @@ SIGNATURES = {
     "spatten_decode_attend": (c_int, [ctypes.POINTER(DecodeArgs), c_vp, ctypes.c_size_t, c_vp]),
     "spatten_qkv_proj": (c_int, [ctypes.POINTER(QkvProjArgs), c_vp]),
     "spatten_qk_norm_rope": (c_int, [ctypes.POINTER(QkNormRopeArgs), c_vp]),
+    "spatten_compact_out_proj": (c_int, [ctypes.POINTER(CompactOutProjArgs), c_vp]),
     "spatten_gather_rows": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_int, c_int, c_int,
                                     c_i64, c_i64, c_vp, c_i64, c_i64, c_vp]),
 }

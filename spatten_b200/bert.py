@@ -44,10 +44,11 @@ import torch
 import torch.nn.functional as F
 from transformers.modeling_outputs import BaseModelOutputWithPastAndCrossAttentions
 from transformers.models.bert.modeling_bert import BertEncoder, BertSelfAttention
+from transformers.pytorch_utils import apply_chunking_to_forward
 
 from . import _native as N
 from .progressive import prog_attn, quant_k_planes, quant_q_int8
-from .proj import qkv_proj
+from .proj import compact_out_proj, qkv_proj
 from .select import gather_head_rows, gather_rows, topk_indices
 
 
@@ -110,6 +111,9 @@ class SpattenBertSelfAttention(BertSelfAttention):
         # batch sharded over ranks: all-reduce head importance over this group
         # (the reference's head decision is batch-global)
         self.process_group = None
+        # encoder loop: run this layer's output projection, LayerNorm and FFN
+        # on the tokens the next layer keeps only (fp16 / bf16, eval mode)
+        self.compact_ffn = True
         # diagnostics of the last forward
         self.last_refetch = None
         self.last_head_importance = None
@@ -217,17 +221,59 @@ class SpattenBertSelfAttention(BertSelfAttention):
         return (full.view(B, S, H * d), None)
 
 
+def _compactable(layer, attn, hidden_states, last):
+    """Whether the layer's tail (output projection, LayerNorm, FFN) can run on
+    the kept tokens only: a row-wise tail in eval mode (no dropout), fp16 /
+    bf16, head_dim a multiple of 64, hidden a multiple of 32, and a next layer
+    to take the compacted rows."""
+    if last or attn.training or not getattr(attn, "compact_ffn", False) or not attn.enable_token_prune:
+        return False
+    if getattr(layer, "is_decoder", False) or not hasattr(layer, "feed_forward_chunk"):
+        return False
+    so = getattr(layer.attention, "output", None)
+    if so is None or not hasattr(so, "dense") or not hasattr(so, "LayerNorm"):
+        return False
+    return (hidden_states.is_cuda and hidden_states.dtype in (torch.float16, torch.bfloat16)
+            and so.dense.weight.dtype == hidden_states.dtype and attn.head_dim % 64 == 0
+            and hidden_states.shape[-1] % 32 == 0)
+
+
+def _layer_tail(layer, attn, ctx, hidden_states, kept):
+    """HF BertLayer after its self-attention (BertSelfOutput, then the FFN
+    chunk). With ``kept`` the next layer's token gather (module.py:49-54)
+    runs first, folded into the output projection's row loads
+    (``compact_out_proj``): every step of the tail is row-wise, so its rows
+    for the kept tokens are the reference's rows, and the FFN skips the rows
+    the next layer drops."""
+    so = layer.attention.output
+    if kept is None:
+        a = so(ctx, hidden_states)
+    else:
+        y = compact_out_proj(ctx, hidden_states, kept, so.dense.weight, so.dense.bias,
+                             attn.num_heads, attn.head_dim, heads=attn.active_head_indices_for_this_layer)
+        a = so.LayerNorm(y)
+    return apply_chunking_to_forward(layer.feed_forward_chunk, layer.chunk_size_feed_forward,
+                                     layer.seq_len_dim, a)
+
+
 def spatten_encoder_forward(self, hidden_states, attention_mask=None, **kwargs):
     """Cascade encoder loop (module.py:40-99): per layer, compact the kept
     tokens' hidden states, key mask and cumulative score, hand the active
     heads and the score to the attention module, run the layer, and read its
-    decisions back."""
+    decisions back. In eval mode on fp16 / bf16 a layer whose attention chose
+    the next layer's tokens runs its tail on those tokens only
+    (``_layer_tail``), so the next layer's hidden states arrive compacted and
+    are not gathered again (``compact_ffn = False`` on the attention module
+    turns this off)."""
     active_heads = None
     active_tokens = None
     cumulative = None
-    for layer in self.layer:
+    compacted = False
+    n_layers = len(self.layer)
+    for i, layer in enumerate(self.layer):
         if active_tokens is not None:
-            hidden_states = gather_rows(hidden_states, active_tokens)
+            if not compacted:
+                hidden_states = gather_rows(hidden_states, active_tokens)
             if attention_mask is not None:
                 m = attention_mask
                 if m.dim() == 4:      # [B, 1, Sq, Sk] -> key mask of query row 0, [B, 1, 1, K]
@@ -239,8 +285,15 @@ def spatten_encoder_forward(self, hidden_states, attention_mask=None, **kwargs):
         attn = layer.attention.self
         attn.active_head_indices_for_this_layer = active_heads
         attn.cumulative_token_score = cumulative
-        out = layer(hidden_states, attention_mask=attention_mask, **kwargs)
-        hidden_states = out[0] if isinstance(out, (tuple, list)) else out
+        if _compactable(layer, attn, hidden_states, last=(i == n_layers - 1)):
+            ctx, _ = attn(hidden_states, attention_mask=attention_mask, **kwargs)
+            kept = attn.next_active_token_indices
+            hidden_states = _layer_tail(layer, attn, ctx, hidden_states, kept)
+            compacted = kept is not None
+        else:
+            out = layer(hidden_states, attention_mask=attention_mask, **kwargs)
+            hidden_states = out[0] if isinstance(out, (tuple, list)) else out
+            compacted = False
         active_heads = attn.next_active_head_indices
         active_tokens = attn.next_active_token_indices
         cumulative = attn.cumulative_token_score

@@ -84,10 +84,12 @@ const char* spatten_last_error(void) { return g_err.c_str(); }
 
 int spatten_device_error(unsigned int* code, int reset) {
   if (!code) return fail(SPATTEN_ERR_INVALID, "device_error: null output");
-  unsigned int proj = 0;
+  unsigned int proj = 0, out = 0;
   if (int e = cuda_status(spatten::read_device_error(code, reset != 0), "device_error read")) return e;
   if (int e = cuda_status(spatten::read_proj_device_error(&proj, reset != 0), "device_error read")) return e;
+  if (int e = cuda_status(spatten::read_out_proj_device_error(&out, reset != 0), "device_error read")) return e;
   if (*code == 0) *code = proj;
+  if (*code == 0) *code = out;
   return ok();
 }
 
@@ -428,6 +430,40 @@ int spatten_qk_norm_rope(const spatten_qk_norm_rope_args* a, void* stream) {
   p.q_out = a->q_out; p.qo_st = a->q_out_row_stride;
   p.q8 = a->q8; p.q_scale = a->q_scale;
   return cuda_status(spatten::launch_qk_prep(p, (cudaStream_t)stream), "qk_norm_rope launch");
+}
+
+int spatten_compact_out_proj(const spatten_compact_out_proj_args* a, void* stream) {
+  if (!a) return fail(SPATTEN_ERR_INVALID, "compact_out_proj: null args");
+  if (a->dtype != SPATTEN_DTYPE_F16 && a->dtype != SPATTEN_DTYPE_BF16)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "compact_out_proj: dtype %d (need f16 or bf16)", a->dtype);
+  if (a->B < 1 || a->S < 1 || a->L < 1 || a->N < 1 || a->H < 1 || a->cur < 1 || a->cur > a->H)
+    return fail(SPATTEN_ERR_INVALID, "compact_out_proj: bad sizes B=%d S=%d L=%d N=%d H=%d cur=%d", a->B, a->S,
+                a->L, a->N, a->H, a->cur);
+  if (a->head_dim < 64 || a->head_dim % 64)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "compact_out_proj: head_dim %d (need a multiple of 64)", a->head_dim);
+  if (a->N % 32) return fail(SPATTEN_ERR_UNSUPPORTED, "compact_out_proj: N %d not a multiple of 32", a->N);
+  if ((int64_t)a->B * a->S > ((int64_t)1 << 31) - 1 || (int64_t)a->B * a->L > ((int64_t)1 << 31) - 1 ||
+      (int64_t)a->H * a->head_dim > ((int64_t)1 << 30))
+    return fail(SPATTEN_ERR_UNSUPPORTED, "compact_out_proj: too many rows or columns");
+  if (!a->kept || !a->ctx || !a->w || !a->res || !a->out)
+    return fail(SPATTEN_ERR_INVALID, "compact_out_proj: null kept/ctx/w/res/out");
+  if (a->ctx_row_stride < (int64_t)a->H * a->head_dim || a->res_row_stride < a->N)
+    return fail(SPATTEN_ERR_INVALID, "compact_out_proj: row stride shorter than the row");
+  if (a->ctx_row_stride % 8 || a->res_row_stride % 8)
+    return fail(SPATTEN_ERR_INVALID, "compact_out_proj: strides must be multiples of 8 elements");
+  if (!aligned(a->ctx, 16) || !aligned(a->w, 16) || !aligned(a->res, 16) || !aligned(a->out, 16) ||
+      (a->bias && !aligned(a->bias, 16)) || !aligned(a->kept, 8) || (a->heads && !aligned(a->heads, 8)))
+    return fail(SPATTEN_ERR_INVALID, "compact_out_proj: a pointer is misaligned");
+  spatten::OutProjParams p;
+  p.dtype = a->dtype;
+  p.B = a->B; p.S = a->S; p.L = a->L; p.N = a->N;
+  p.H = a->H; p.Dh = a->head_dim; p.cur = a->cur;
+  p.heads = a->heads; p.kept = a->kept;
+  p.ctx = a->ctx; p.ctx_st = a->ctx_row_stride;
+  p.w = a->w; p.bias = a->bias;
+  p.res = a->res; p.res_st = a->res_row_stride;
+  p.out = a->out;
+  return cuda_status(spatten::launch_out_proj(p, (cudaStream_t)stream), "compact_out_proj launch");
 }
 
 }  // extern "C"

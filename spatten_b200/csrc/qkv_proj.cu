@@ -353,8 +353,10 @@ __global__ void __launch_bounds__(kThreads, 1) qkv_proj_kernel(const __grid_cons
   }
 }
 
+}  // namespace
+
 // ---------------------------------------------------------------- host side
-PFN_cuTensorMapEncodeTiled_v12000 proj_encode_fn() {
+static PFN_cuTensorMapEncodeTiled_v12000 proj_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
     void* ptr = nullptr;
@@ -379,6 +381,8 @@ cudaError_t make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
+
+namespace {
 
 template <typename T>
 cudaError_t launch_proj_t(const ProjParams& a, cudaStream_t st) {

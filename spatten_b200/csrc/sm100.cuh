@@ -14,7 +14,7 @@ namespace sm100 {
 // Device error word: a kernel whose wait runs out of time records where it gave
 // up here (first writer wins) and returns instead of spinning forever. The
 // word is static: each translation unit that includes this header
-// (prog_attn_tc.cu, qkv_proj.cu) has its own and reads it back for
+// (prog_attn_tc.cu, qkv_proj.cu, out_proj.cu) has its own and reads it back for
 // spatten_device_error().
 // ---------------------------------------------------------------------------
 static __device__ unsigned int g_device_error = 0;

@@ -88,3 +88,61 @@ def qkv_proj(x, w, bias, num_heads, head_dim, heads=None, quantize=True):
     a.q, a.k = q.data_ptr(), k.data_ptr()
     N.check(N.lib.spatten_qkv_proj(a, _stream(x)))
     return QkvDense(q, k, v)
+
+
+def compact_out_proj(ctx, res, kept, w, bias, num_heads, head_dim, heads=None):
+    """Attention output projection + residual of the kept tokens only
+    (host side of spatten_compact_out_proj): the gather of the next layer's
+    hidden states (module.py:49-54) moved into the row loads of HF
+    BertSelfOutput's dense layer, so what follows runs on the compacted rows.
+
+        out[b, j] = T(T(ctx[b, s] @ w.T + bias) + res[b, s]),  s = kept[b, j]
+
+    ctx  [B, S, num_heads * head_dim] (the attention context; only the
+         ``heads`` column blocks are read, the others must be zero for the
+         result to equal the dense layer's)
+    res  [B, S, N] (the layer's input hidden states)
+    kept int64 [B, L] positions; w [N, num_heads * head_dim]; bias [N] or None
+    returns [B, L, N] in ctx's dtype."""
+    if not (ctx.is_cuda and res.is_cuda and w.is_cuda and kept.is_cuda):
+        raise ValueError("compact_out_proj takes CUDA tensors; there is no CPU path")
+    if ctx.dtype not in (torch.float16, torch.bfloat16) or w.dtype != ctx.dtype or res.dtype != ctx.dtype:
+        raise ValueError("compact_out_proj: ctx, res and w must share one dtype, fp16 or bf16")
+    if ctx.dim() != 3 or res.dim() != 3 or kept.dim() != 2:
+        raise ValueError("compact_out_proj: ctx, res must be [B, S, F], kept [B, L]")
+    B, S, F = ctx.shape
+    Nf = w.shape[0]
+    if F != num_heads * head_dim or tuple(w.shape) != (Nf, F) or tuple(res.shape) != (B, S, Nf) \
+            or kept.shape[0] != B:
+        raise ValueError(f"compact_out_proj: shapes ctx {tuple(ctx.shape)}, res {tuple(res.shape)}, "
+                         f"w {tuple(w.shape)}, kept {tuple(kept.shape)} do not match")
+    if ctx.stride(2) != 1 or ctx.stride(0) != S * ctx.stride(1):
+        ctx = ctx.contiguous()
+    if res.stride(2) != 1 or res.stride(0) != S * res.stride(1):
+        res = res.contiguous()
+    w = w.contiguous()
+    kept = kept.to(torch.int64).contiguous()
+    if bias is not None:
+        bias = bias.contiguous()
+        if bias.dtype != ctx.dtype or bias.numel() != Nf:
+            raise ValueError("compact_out_proj: bias must match w's rows and ctx's dtype")
+    if heads is not None:
+        heads = heads.to(torch.int64).contiguous()
+        cur = heads.numel()
+    else:
+        cur = num_heads
+    L = kept.shape[1]
+    out = torch.empty(B, L, Nf, dtype=ctx.dtype, device=ctx.device)
+    a = N.CompactOutProjArgs()
+    a.dtype = _DT[ctx.dtype]
+    a.B, a.S, a.L, a.N = B, S, L, Nf
+    a.H, a.head_dim, a.cur = num_heads, head_dim, cur
+    a.heads = heads.data_ptr() if heads is not None else None
+    a.kept = kept.data_ptr()
+    a.ctx, a.ctx_row_stride = ctx.data_ptr(), ctx.stride(1)
+    a.w = w.data_ptr()
+    a.bias = bias.data_ptr() if bias is not None else None
+    a.res, a.res_row_stride = res.data_ptr(), res.stride(1)
+    a.out = out.data_ptr()
+    N.check(N.lib.spatten_compact_out_proj(a, _stream(ctx)))
+    return out

@@ -212,3 +212,30 @@ def test_qk_norm_rope_args_validation():
     assert N.lib.spatten_qk_norm_rope(a, None) == N.ERR_INVALID
     a.q_row_stride, a.k = 2048, (1 << 20) + 4
     assert N.lib.spatten_qk_norm_rope(a, None) == N.ERR_INVALID
+
+
+def test_compact_out_proj_args_validation():
+    """The kept-token output projection rejects bad arguments before any
+    launch."""
+    from spatten_b200 import _native as N
+    assert N.lib.spatten_compact_out_proj(None, None) == N.ERR_INVALID
+    a = N.CompactOutProjArgs()
+    a.dtype, a.B, a.S, a.L, a.N, a.H, a.head_dim, a.cur = N.DTYPE_F16, 4, 512, 461, 768, 12, 64, 10
+    a.ctx = a.w = a.res = a.out = 1 << 20
+    a.ctx_row_stride, a.res_row_stride = 768, 768
+    assert N.lib.spatten_compact_out_proj(a, None) == N.ERR_INVALID  # kept missing
+    a.kept = 1 << 21
+    a.dtype = N.DTYPE_F32
+    assert N.lib.spatten_compact_out_proj(a, None) == N.ERR_UNSUPPORTED
+    a.dtype, a.head_dim = N.DTYPE_BF16, 96
+    assert N.lib.spatten_compact_out_proj(a, None) == N.ERR_UNSUPPORTED
+    a.head_dim, a.N = 64, 100  # features not a multiple of 32
+    assert N.lib.spatten_compact_out_proj(a, None) == N.ERR_UNSUPPORTED
+    a.N, a.cur = 768, 13  # more active heads than the context row has
+    assert N.lib.spatten_compact_out_proj(a, None) == N.ERR_INVALID
+    a.cur, a.ctx_row_stride = 10, 700
+    assert N.lib.spatten_compact_out_proj(a, None) == N.ERR_INVALID
+    a.ctx_row_stride, a.res = 768, (1 << 20) + 8  # residual not 16-byte aligned
+    assert N.lib.spatten_compact_out_proj(a, None) == N.ERR_INVALID
+    a.res, a.L = 1 << 20, 0
+    assert N.lib.spatten_compact_out_proj(a, None) == N.ERR_INVALID

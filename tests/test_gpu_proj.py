@@ -108,3 +108,48 @@ def test_qkv_proj_dense_matches_torch(dt):
         ref = torch.nn.functional.linear(x, w[rows], b[rows])
         ref = ref.view(B, S, heads.numel(), D).permute(0, 2, 1, 3)
         torch.testing.assert_close(got.float(), ref.float(), rtol=RTOL[dt], atol=2e-3)
+
+
+# --- attention output projection of the kept tokens (spatten_compact_out_proj) ----
+
+OUT_CASES = [
+    # B, S, L (kept), H, D, N (features), active heads (None = all), dtype, bias
+    (2, 300, 270, 12, 64, 768, [0, 2, 3, 5, 6, 7, 8, 9, 10, 11, 1], torch.float16, True),
+    (3, 77, 70, 8, 128, 1024, None, torch.bfloat16, True),
+    (1, 200, 131, 4, 64, 96, [3, 1], torch.float16, False),  # partial row and feature tiles
+    (2, 64, 1, 12, 64, 768, None, torch.bfloat16, True),     # one kept token per sequence
+    (4, 512, 461, 12, 64, 768, [4, 0, 9, 2, 11, 7, 5, 1, 10, 3], torch.float16, True),
+]
+OUT_ATOL = {torch.float16: 4e-3, torch.bfloat16: 3e-2}
+
+
+@pytest.mark.parametrize("case", OUT_CASES)
+def test_compact_out_proj_matches_torch(case):
+    """Against the unfused layer in torch fp32 (dense over the whole context
+    row, rounded where the dense layer and the residual add round) followed
+    by the gather of the kept rows: within one or two ulps, most elements
+    identical."""
+    from spatten_b200.proj import compact_out_proj
+    B, S, L, H, D, Nf, heads, dt, bias = case
+    g = torch.Generator().manual_seed(S + L + Nf)
+    ctx = torch.randn(B, S, H, D, generator=g)
+    if heads is not None:  # pruned heads' blocks are zeros in the drop-in's context
+        off = torch.ones(H, dtype=torch.bool)
+        off[heads] = False
+        ctx[:, :, off] = 0
+    ctx = ctx.reshape(B, S, H * D).to(dt)
+    res = torch.randn(B, S, Nf, generator=g).to(dt)
+    w = (torch.randn(Nf, H * D, generator=g) / (H * D) ** 0.5).to(dt)
+    b = (torch.randn(Nf, generator=g) * 0.1).to(dt) if bias else None
+    kept = torch.sort(torch.stack([torch.randperm(S, generator=g)[:L] for _ in range(B)]), dim=1).values
+    out = compact_out_proj(ctx.cuda(), res.cuda(), kept.cuda(), w.cuda(), None if b is None else b.cuda(),
+                           H, D, heads=None if heads is None else torch.tensor(heads).cuda())
+    y = ctx.float() @ w.float().T
+    if b is not None:
+        y = y + b.float()
+    y = (y.to(dt).float() + res.float()).to(dt)
+    ref = torch.gather(y, 1, kept[:, :, None].expand(-1, -1, Nf))
+    assert out.shape == (B, L, Nf) and out.dtype == dt
+    got = out.cpu()
+    torch.testing.assert_close(got.float(), ref.float(), rtol=2 * RTOL[dt], atol=OUT_ATOL[dt])
+    assert (got == ref).float().mean().item() > 0.97
