@@ -314,6 +314,7 @@ def patch_bert(model, **knobs):
         new.load_state_dict(old.state_dict())
         new.layer_id = i
         new.to(device=old.query.weight.device, dtype=old.query.weight.dtype)
+        new.train(old.training)  # a fresh module is in training mode; keep the model's
         for k, v in knobs.items():
             setattr(new, k, v)
         layer.attention.self = new

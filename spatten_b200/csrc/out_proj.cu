@@ -24,13 +24,17 @@
 //   warp 1      MMA issuer + TMEM owner: kind::f16 into one of two fp32
 //               accumulators of 128 columns (double-buffered: the next tile's
 //               MMAs overlap this tile's epilogue);
-//   warps 2-5   row gather: one tile row per thread, eight 16-byte cp.async
-//               per K step from the kept row's context, written in the
-//               128-byte swizzled K-major layout the MMA reads; a stage is
-//               released kLag K steps later, after cp.async.wait_group and a
-//               proxy fence (generic writes -> async-proxy reads);
+//   warps 2-5   row gather: 32 tile rows per warp, eight lanes per row (one
+//               16-byte cp.async each, so a warp instruction reads four whole
+//               128-byte rows) per K step from the kept rows' context, written
+//               in the 128-byte swizzled K-major layout the MMA reads; a stage
+//               is released kLag K steps later, after cp.async.wait_group and
+//               a proxy fence (generic writes -> async-proxy reads);
 //   warps 6-13  epilogue, two warps per TMEM lane quarter (64 columns each):
-//               + bias, round, + the kept row's residual, round, 16-byte stores.
+//               + bias and rounding in the TMEM layout (a row per lane), then
+//               through a per-warp shared-memory tile to a layout of four
+//               lanes per 64-byte row segment, where the kept row's residual
+//               is read and the sum stored with 16-byte accesses.
 // Every wait is bounded; a timeout records a code in this file's device error
 // word, the CTA lets its copies and MMAs land and returns.
 #include <cuda.h>
@@ -69,21 +73,19 @@ struct OutLayout {
   static constexpr int kNumBars = 2 * kStages + 5;
   static constexpr int oTmem = oBar + kNumBars * 8;
   static constexpr int oAbort = oTmem + 4;
-  static constexpr int kBytes = oAbort + 12;
+  static constexpr int kEpiStride = 80;                  // bytes per staged row: 32 values + 16 pad
+  static constexpr int oEpi = (oAbort + 12 + 15) & ~15;  // [kEpiWarps][32 rows][kEpiStride], 16-byte aligned
+  static constexpr int kBytes = oEpi + kEpiWarps * 32 * kEpiStride;
   static constexpr int kAlloc = kBytes + 1024;
 };
 static_assert(OutLayout::kAlloc <= 227 * 1024, "shared memory");
+static_assert(OutLayout::oEpi % 16 == 0 && OutLayout::kEpiStride % 16 == 0, "16-byte staging rows");
 static_assert(OM == kGatherWarps * 32, "one gather thread per tile row");
 
 struct OutKParams {
   OutProjParams a;
   CUtensorMap tm_w;  // [N, H * Dh], box {64, 128}
 };
-
-template <typename T>
-SPATTEN_DEV float round_to(float x) {
-  return to_f32<T>(from_f32<T>(x));
-}
 
 // input row (b * S + s) of output row gr (< B * L); kept positions are caller
 // data, clamped into the sequence
@@ -199,23 +201,32 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
       }
     }
   } else if (warp < 2 + kGatherWarps) {
-    // row gather: thread r copies tile row r (128 bytes per K step)
-    const int r = (warp - 2) * 32 + lane;
+    // row gather: warp gw fills tile rows gw*32 .. gw*32+31, lane = (row
+    // sub-index, 16-byte chunk); one instruction covers rows i*4 .. i*4+3
+    const int gw = warp - 2, sub = lane >> 3, ch = lane & 7;
     const T* ctx = static_cast<const T*>(p.ctx);
     int g = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-      const int gr = (t / nt) * OM + r;
-      // rows past the end copy input row 0 (their results are not stored)
-      const T* row = ctx + (gr < M ? src_row(p, gr) : 0) * p.ctx_st;
+      const int m0 = (t / nt) * OM;
+      const T* row[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int gr = m0 + gw * 32 + i * 4 + sub;
+        // rows past the end copy input row 0 (their results are not stored)
+        row[i] = ctx + (gr < M ? src_row(p, gr) : 0) * p.ctx_st + ch * 8;
+      }
       for (int kb = 0; kb < KT; ++kb, ++g) {
         const int s = g % kStages;
         const bool w = mbar_wait(&empty[s], ((g / kStages) & 1) ^ 1, kErrOut | 5, abort);
         if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
-        uint8_t* dst = sm + Lay::oStage + s * Lay::kStageBytes + r * 128;
-        const T* src = row + k_col(p, kb);
+        uint8_t* st = sm + Lay::oStage + s * Lay::kStageBytes;
+        const int col = k_col(p, kb);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) cp_async16(dst + ((c ^ (r & 7)) << 4), src + c * 8, true);
+        for (int i = 0; i < 8; ++i) {
+          const int r = gw * 32 + i * 4 + sub;
+          cp_async16(st + r * 128 + ((ch ^ (r & 7)) << 4), row[i] + col, true);
+        }
         cp_async_commit();
         if (g >= kLag) {
           cp_async_wait<kLag>();
@@ -232,11 +243,12 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
       for (int u = (g > kLag ? g - kLag : 0); u < g; ++u) mbar_arrive(&full[u % kStages]);
   } else {
     const int e = warp - 2 - kGatherWarps, half = e >> 2, qd = warp & 3;
-    const int r = qd * 32 + lane;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const T* bias = static_cast<const T*>(p.bias);
     const T* res = static_cast<const T*>(p.res);
     T* out = static_cast<T*>(p.out);
+    uint8_t* stg = sm + Lay::oEpi + e * 32 * Lay::kEpiStride;
+    const int cq = lane & 3;  // 16-byte column chunk of the store layout
     int lt = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
@@ -244,9 +256,14 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
       ok = __all_sync(0xffffffffu, ok && !*abort);
       if (!ok) break;
       tc_fence_after();
-      const int gr = (t / nt) * OM + r;
-      const bool valid = gr < M;
-      const T* rrow = res + (valid ? src_row(p, gr) : 0) * p.res_st;
+      // store layout: lane handles rows (lane >> 2) + 8 i of the warp's 32
+      const int m0 = (t / nt) * OM + qd * 32;
+      int64_t rsrc[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int gr = m0 + (lane >> 2) + 8 * i;
+        rsrc[i] = gr < M ? src_row(p, gr) : -1;
+      }
       for (int cc = half * (ON / 2); cc < (half + 1) * (ON / 2); cc += 32) {
         const int n = (t % nt) * ON + cc;
         if (n >= p.N) break;  // warp-uniform: N is a multiple of 32
@@ -254,25 +271,36 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
         __syncwarp();
         tmem_ld32(tmem + lane_base + buf * ON + cc, a);
         tmem_wait_ld();
-        if (valid) {
-          uint4 rv[4], bv[4];
+        // TMEM layout (lane = row): y = T(acc + bias), staged as 64 bytes of the row
+        uint4 bv[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            rv[i] = __ldg(reinterpret_cast<const uint4*>(rrow + n) + i);
-            bv[i] = bias ? __ldg(reinterpret_cast<const uint4*>(bias + n) + i) : make_uint4(0u, 0u, 0u, 0u);
-          }
-          const T* re = reinterpret_cast<const T*>(rv);
-          const T* be = reinterpret_cast<const T*>(bv);
-          uint32_t pk[16];
+        for (int i = 0; i < 4; ++i)
+          bv[i] = bias ? __ldg(reinterpret_cast<const uint4*>(bias + n) + i) : make_uint4(0u, 0u, 0u, 0u);
+        const T* be = reinterpret_cast<const T*>(bv);
+        uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float y0 = round_to<T>(__uint_as_float(a[2 * i]) + to_f32<T>(be[2 * i]));
-            const float y1 = round_to<T>(__uint_as_float(a[2 * i + 1]) + to_f32<T>(be[2 * i + 1]));
-            pk[i] = pack2<T>(y0 + to_f32<T>(re[2 * i]), y1 + to_f32<T>(re[2 * i + 1]));
-          }
-          uint4* d4 = reinterpret_cast<uint4*>(out + (int64_t)gr * p.N + n);
+        for (int i = 0; i < 16; ++i)
+          pk[i] = pack2<T>(__uint_as_float(a[2 * i]) + to_f32<T>(be[2 * i]),
+                           __uint_as_float(a[2 * i + 1]) + to_f32<T>(be[2 * i + 1]));
+        uint4* srow = reinterpret_cast<uint4*>(stg + lane * Lay::kEpiStride);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        for (int i = 0; i < 4; ++i) srow[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        __syncwarp();
+        // store layout: out = T(y + residual), 16 bytes per lane
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (rsrc[i] < 0) continue;
+          const int rr = (lane >> 2) + 8 * i;
+          const uint4 yv = *reinterpret_cast<const uint4*>(stg + rr * Lay::kEpiStride + cq * 16);
+          const uint4 rv = __ldg(reinterpret_cast<const uint4*>(res + rsrc[i] * p.res_st + n + cq * 8));
+          const T* ye = reinterpret_cast<const T*>(&yv);
+          const T* re = reinterpret_cast<const T*>(&rv);
+          uint32_t o[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            o[k] = pack2<T>(to_f32<T>(ye[2 * k]) + to_f32<T>(re[2 * k]),
+                            to_f32<T>(ye[2 * k + 1]) + to_f32<T>(re[2 * k + 1]));
+          *reinterpret_cast<uint4*>(out + (int64_t)(m0 + rr) * p.N + n + cq * 8) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
       tc_fence_before();
