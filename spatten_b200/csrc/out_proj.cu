@@ -63,6 +63,7 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = (2 + kGatherWarps + kEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 2 * ON;
 constexpr unsigned kErrOut = 0x300;
+constexpr int kMaxKT = 256;  // K steps whose first column is tabled in shared memory
 
 struct OutLayout {
   static constexpr int kABytes = OM * OK * 2;
@@ -75,12 +76,14 @@ struct OutLayout {
   static constexpr int oAbort = oTmem + 4;
   static constexpr int kEpiStride = 80;                  // bytes per staged row: 32 values + 16 pad
   static constexpr int oEpi = (oAbort + 12 + 15) & ~15;  // [kEpiWarps][32 rows][kEpiStride], 16-byte aligned
-  static constexpr int kBytes = oEpi + kEpiWarps * 32 * kEpiStride;
+  static constexpr int oKcol = oEpi + kEpiWarps * 32 * kEpiStride;  // int [kMaxKT]: first column of each K step
+  static constexpr int kBytes = oKcol + kMaxKT * 4;
   static constexpr int kAlloc = kBytes + 1024;
 };
 static_assert(OutLayout::kAlloc <= 227 * 1024, "shared memory");
 static_assert(OutLayout::oEpi % 16 == 0 && OutLayout::kEpiStride % 16 == 0, "16-byte staging rows");
-static_assert(OM == kGatherWarps * 32, "one gather thread per tile row");
+static_assert(OM == kGatherWarps * 32, "32 tile rows per gather warp");
+static_assert(ON == 128, "epilogue: two 32-column chunks per warp half");
 
 struct OutKParams {
   OutProjParams a;
@@ -142,6 +145,9 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
     tmem_alloc(tslot, kTmemCols);
     tmem_relinquish();
   }
+  int* kcol_s = reinterpret_cast<int*>(sm + Lay::oKcol);
+  for (int kb = threadIdx.x; kb < KT && kb < kMaxKT; kb += blockDim.x) kcol_s[kb] = k_col(p, kb);
+  auto kcol = [&](int kb) { return kb < kMaxKT ? kcol_s[kb] : k_col(p, kb); };
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -158,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
           const int s = g % kStages;
           if (!mbar_wait(&empty[s], ((g / kStages) & 1) ^ 1, kErrOut | 1, abort)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], Lay::kBBytes);
-          tma_load_2d(sm + Lay::oStage + s * Lay::kStageBytes + Lay::kABytes, &P.tm_w, k_col(p, kb), n0,
+          tma_load_2d(sm + Lay::oStage + s * Lay::kStageBytes + Lay::kABytes, &P.tm_w, kcol(kb), n0,
                       &full[s]);
         }
       }
@@ -205,23 +211,31 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
     // sub-index, 16-byte chunk); one instruction covers rows i*4 .. i*4+3
     const int gw = warp - 2, sub = lane >> 3, ch = lane & 7;
     const T* ctx = static_cast<const T*>(p.ctx);
+    // input rows of tile t's kept rows (rows past the end copy input row 0;
+    // their results are not stored); the next tile's are loaded while this
+    // tile's K steps run
+    auto rows_of = [&](int t, int64_t (&src)[8]) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int gr = (t / nt) * OM + gw * 32 + i * 4 + sub;
+        src[i] = (t < ntiles && gr < M) ? src_row(p, gr) : 0;
+      }
+    };
+    int64_t src[8], nsrc[8];
+    rows_of(blockIdx.x, src);
     int g = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-      const int m0 = (t / nt) * OM;
       const T* row[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int gr = m0 + gw * 32 + i * 4 + sub;
-        // rows past the end copy input row 0 (their results are not stored)
-        row[i] = ctx + (gr < M ? src_row(p, gr) : 0) * p.ctx_st + ch * 8;
-      }
+      for (int i = 0; i < 8; ++i) row[i] = ctx + src[i] * p.ctx_st + ch * 8;
+      rows_of(t + gridDim.x, nsrc);
       for (int kb = 0; kb < KT; ++kb, ++g) {
         const int s = g % kStages;
         const bool w = mbar_wait(&empty[s], ((g / kStages) & 1) ^ 1, kErrOut | 5, abort);
         if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
         uint8_t* st = sm + Lay::oStage + s * Lay::kStageBytes;
-        const int col = k_col(p, kb);
+        const int col = kcol(kb);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int r = gw * 32 + i * 4 + sub;
@@ -235,6 +249,8 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
           if (lane == 0) mbar_arrive(&full[(g - kLag) % kStages]);
         }
       }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) src[i] = nsrc[i];
     }
     cp_async_wait<0>();
     fence_proxy_async_smem();
@@ -252,11 +268,8 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
     int lt = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
-      bool ok = mbar_wait(&acc_full[buf], (lt >> 1) & 1, kErrOut | 3, abort);
-      ok = __all_sync(0xffffffffu, ok && !*abort);
-      if (!ok) break;
-      tc_fence_after();
-      // store layout: lane handles rows (lane >> 2) + 8 i of the warp's 32
+      // store layout: lane handles rows (lane >> 2) + 8 i of the warp's 32;
+      // their residual segments are loaded before the accumulator is waited for
       const int m0 = (t / nt) * OM + qd * 32;
       int64_t rsrc[4];
 #pragma unroll
@@ -264,7 +277,23 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
         const int gr = m0 + (lane >> 2) + 8 * i;
         rsrc[i] = gr < M ? src_row(p, gr) : -1;
       }
-      for (int cc = half * (ON / 2); cc < (half + 1) * (ON / 2); cc += 32) {
+      uint4 rv[2][4];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int n = (t % nt) * ON + half * (ON / 2) + c * 32;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          rv[c][i] = (rsrc[i] >= 0 && n < p.N)
+                         ? __ldg(reinterpret_cast<const uint4*>(res + rsrc[i] * p.res_st + n + cq * 8))
+                         : make_uint4(0u, 0u, 0u, 0u);
+      }
+      bool ok = mbar_wait(&acc_full[buf], (lt >> 1) & 1, kErrOut | 3, abort);
+      ok = __all_sync(0xffffffffu, ok && !*abort);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int cc = half * (ON / 2) + c * 32;
         const int n = (t % nt) * ON + cc;
         if (n >= p.N) break;  // warp-uniform: N is a multiple of 32
         uint32_t a[32];
@@ -292,9 +321,8 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
           if (rsrc[i] < 0) continue;
           const int rr = (lane >> 2) + 8 * i;
           const uint4 yv = *reinterpret_cast<const uint4*>(stg + rr * Lay::kEpiStride + cq * 16);
-          const uint4 rv = __ldg(reinterpret_cast<const uint4*>(res + rsrc[i] * p.res_st + n + cq * 8));
           const T* ye = reinterpret_cast<const T*>(&yv);
-          const T* re = reinterpret_cast<const T*>(&rv);
+          const T* re = reinterpret_cast<const T*>(&rv[c][i]);
           uint32_t o[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k)
