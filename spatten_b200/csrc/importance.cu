@@ -23,7 +23,16 @@ __global__ void tok_reduce_kernel(const float* __restrict__ part, int Z, int H, 
   const float* p = part + (int64_t)z * H * mtiles * stride + n;
   double acc = 0.0;
   const int cnt = H * mtiles;
-  for (int i = 0; i < cnt; ++i) acc += (double)__ldg(p + (int64_t)i * stride);
+  // batches of 16 loads in flight, summed in the same fixed order
+  int i = 0;
+  for (; i + 16 <= cnt; i += 16) {
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __ldg(p + (int64_t)(i + j) * stride);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc += (double)v[j];
+  }
+  for (; i < cnt; ++i) acc += (double)__ldg(p + (int64_t)i * stride);
   float r = (float)acc;
   if (tok_in) r = tok_in[(int64_t)z * N + n] + r;
   tok_out[(int64_t)z * N + n] = r;
