@@ -17,12 +17,12 @@
 // column blocks are addressed in place.
 //
 // Persistent, warp-specialised: one CTA per SM walks the output tiles
-// (128 kept rows x 128 features, n fastest so the CTAs on one row tile share
+// (128 kept rows x 256 features, n fastest so the CTAs on one row tile share
 // its gathered rows in L2), 14 warps:
-//   warp 0      TMA producer: weight tile [128 x 64] per K step (128B swizzle,
+//   warp 0      TMA producer: weight tile [256 x 64] per K step (128B swizzle,
 //               no multicast) into a kStages ring;
 //   warp 1      MMA issuer + TMEM owner: kind::f16 into one of two fp32
-//               accumulators of 128 columns (double-buffered: the next tile's
+//               accumulators of 256 columns (double-buffered: the next tile's
 //               MMAs overlap this tile's epilogue);
 //   warps 2-5   row gather: 32 tile rows per warp, eight lanes per row (one
 //               16-byte cp.async each, so a warp instruction reads four whole
@@ -30,7 +30,7 @@
 //               in the 128-byte swizzled K-major layout the MMA reads; a stage
 //               is released kLag K steps later, after cp.async.wait_group and
 //               a proxy fence (generic writes -> async-proxy reads);
-//   warps 6-13  epilogue, two warps per TMEM lane quarter (64 columns each):
+//   warps 6-13  epilogue, two warps per TMEM lane quarter (128 columns each):
 //               + bias and rounding in the TMEM layout (a row per lane), then
 //               through a per-warp shared-memory tile to a layout of four
 //               lanes per 64-byte row segment, where the kept row's residual
@@ -54,9 +54,9 @@ namespace {
 using namespace sm100;
 
 constexpr int OM = 128;  // kept rows per tile (TMEM lanes)
-constexpr int ON = 128;  // output features per tile (TMEM columns of one accumulator)
+constexpr int ON = 256;  // output features per tile (TMEM columns of one accumulator)
 constexpr int OK = 64;   // K step: 64 elements = one 128-byte swizzle atom
-constexpr int kStages = 6;
+constexpr int kStages = 4;
 constexpr int kLag = kStages - 2;  // K steps a gather thread keeps in flight before releasing one
 constexpr int kGatherWarps = 4;
 constexpr int kEpiWarps = 8;
@@ -83,11 +83,11 @@ struct OutLayout {
 static_assert(OutLayout::kAlloc <= 227 * 1024, "shared memory");
 static_assert(OutLayout::oEpi % 16 == 0 && OutLayout::kEpiStride % 16 == 0, "16-byte staging rows");
 static_assert(OM == kGatherWarps * 32, "32 tile rows per gather warp");
-static_assert(ON == 128, "epilogue: two 32-column chunks per warp half");
+static_assert(ON == 256, "epilogue: four 32-column chunks per warp half");
 
 struct OutKParams {
   OutProjParams a;
-  CUtensorMap tm_w;  // [N, H * Dh], box {64, 128}
+  CUtensorMap tm_w;  // [N, H * Dh], box {64, 256}
 };
 
 // input row (b * S + s) of output row gr (< B * L); kept positions are caller
@@ -277,9 +277,9 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
         const int gr = m0 + (lane >> 2) + 8 * i;
         rsrc[i] = gr < M ? src_row(p, gr) : -1;
       }
-      uint4 rv[2][4];
+      uint4 rv[4][4];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < 4; ++c) {
         const int n = (t % nt) * ON + half * (ON / 2) + c * 32;
 #pragma unroll
         for (int i = 0; i < 4; ++i)
@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1) out_proj_kernel(const __grid_cons
       if (!ok) break;
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < 4; ++c) {
         const int cc = half * (ON / 2) + c * 32;
         const int n = (t % nt) * ON + cc;
         if (n >= p.N) break;  // warp-uniform: N is a multiple of 32
