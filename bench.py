@@ -5,29 +5,37 @@ Workload (one "step"): the standalone progressive-quantised attention op on
 batch 8 x 12 heads x seq 4096 x head_dim 64, Q/K/V fp16 drawn i.i.d. N(0,1)
 from seed 1 (synthetic, Q then K then V): Q quantised to int8, K to 4-bit
 MSB/LSB planes, exact int8 scores, LSB refetch for rows whose max softmax
-probability is below 0.1, V pruned at p < 1e-3, P.V, token importance [B, S]
-and per-head |O| sums. Inputs (151 MB) exceed the 126 MB L2, so no flush is
-needed between steps.
+probability is below 0.1, V pruned at p < 1e-3, P.V, token importance
+[B, S] and per-head |O| sums, then the cascade's token top-k (keep 0.9 of
+the keys per batch row). Inputs (151 MB) exceed the 126 MB L2, so no flush
+is needed between steps.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 runs under torchrun, one rank per GPU; each rank processes its own
-batch of 8 (weak scaling, no collective on the data path). Rank 0 prints one
-JSON line. ``--impl reference`` times the CPU restatement of the op (the
-reference has no GPU path for it) on rank 0 over a bounded sample.
+N > 1 runs under torchrun, one rank per GPU, on the SAME fixed workload
+(strong scaling): the 96 (batch, head) units are split over the ranks --
+heads over up to 4 ranks (3 heads each), the batch over the rest -- and the
+ranks that share batch rows all-reduce their partial token importance
+(NCCL) before the top-k, the one collective of the data path. Rank 0
+prints one JSON line. ``--impl reference`` times the CPU restatement of the
+op (the reference has no GPU path for it) on rank 0 over a bounded sample.
 
 Besides the op's throughput the line carries: the HBM GB/s of the attention
 launch; a roofline against the measured tensor peak plus the launch's time
 floor (slowest of HBM bytes, int8 + fp16 tensor work and MUFU exp2, with the
 int8 and exp2 rates measured here); the end-to-end rate through the public
 API with pinned host buffers (uploads and downloads overlap the previous /
-next step's compute on their own streams); and the BERT-base SpAtten forward
-in ms per batch (fp16 B32 S512 sharded over the ranks, and fp32 B1 S128 --
-the reference's CPU configuration, which the reference arm times on the host
-cores); the Qwen3-8B decode attention over a 32768-token progressive-quant
-KV cache with top-2048 selection (KV heads split over the ranks) with its HBM
-roofline; and at N=1 the Qwen3-0.6B-architecture prefill (bf16, 4 x 8192,
-cascade pruning of the KV cache) in ms.
+next step's compute on their own streams); at N=1 the op at S in {512, 2048,
+4096, 8192} and on a peaked input (queries close to their own keys, so rows
+are confident and the LSB plane is not fetched); the BERT-base SpAtten
+forward in ms per batch (fp16 B32: S=512 sharded over the ranks; at N=1 also
+S=2048 and 4096 with HF's dense sdpa forward of the same model beside it;
+fp32 B1 S128 -- the reference's CPU configuration, which the reference arm
+times on the host cores); the Qwen3-8B decode attention over a
+32768-token progressive-quant KV cache with top-2048 selection (KV heads
+split over the ranks) with its HBM roofline; and at N=1 the
+Qwen3-0.6B-architecture prefill (bf16, 4 x 8192, cascade pruning of the KV
+cache) in ms.
 """
 import argparse
 import json
@@ -48,7 +56,10 @@ V_THR = 1e-3
 SM_SCALE = 1.0 / math.sqrt(D)
 METRIC = "sparse_attn_tokens_per_s"
 UNIT = "tokens/s"
-LAUNCHES_PER_STEP = 5  # quant Q, quant K planes, attention, token reduce, head reduce
+TOKEN_KEEP = 0.9
+LAUNCHES_PER_STEP = 6  # quant Q, quant K planes, attention, token reduce, head reduce, top-k
+SWEEP_SEQS = (512, 2048, 4096, 8192)
+PEAKED_ALPHA = 1.0
 
 
 def parse():
@@ -59,6 +70,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seq", type=int, default=S)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the sequence sweep and the peaked input")
     ap.add_argument("--no-bert", action="store_true", help="skip the BERT-base ms/batch measurement")
     ap.add_argument("--no-qwen3", action="store_true", help="skip the Qwen3 prefill measurement")
     ap.add_argument("--no-decode", action="store_true", help="skip the Qwen3 decode measurement")
@@ -73,33 +85,50 @@ def parse():
     return ap.parse_args()
 
 
-def config(seq):
-    return {"workload": f"progressive_attention B{B} H{H} S{seq} D{D} fp16 seed{SEED}",
+def config(seq, plan=None):
+    par = "1 GPU" if plan is None or plan.world == 1 else \
+        f"heads over {plan.head_ranks} x batch over {plan.batch_ranks} ranks"
+    return {"workload": f"progressive_attention B{B} H{H} S{seq} D{D} fp16 seed{SEED} + token top-k "
+                        f"(keep {TOKEN_KEEP})",
             "batch": B, "heads": H, "seq_len": seq, "head_dim": D,
-            "refetch_threshold": REFETCH_THR, "v_prune_threshold": V_THR,
-            "l2": "inputs 151 MB > 126 MB L2 (no flush)"}
+            "refetch_threshold": REFETCH_THR, "v_prune_threshold": V_THR, "token_keep": TOKEN_KEEP,
+            "parallelism": par,
+            "l2": "inputs 151 MB > 126 MB L2 at S=4096 (no flush)"}
 
 
-def make_inputs(seed, seq, torch):
+def make_inputs(seed, seq, torch, batch=B):
+    """Q, K, V [batch, 12, seq, 64] fp16, N(0,1) from ``seed`` (Q, K, V in that order)."""
     g = torch.Generator().manual_seed(seed)
-    return [torch.randn(B, H, seq, D, generator=g).half() for _ in range(3)]
+    return [torch.randn(batch, H, seq, D, generator=g).half() for _ in range(3)]
 
 
-def algorithmic_bytes(seq, refetch_frac):
-    """Bytes one attention launch must move: int8 Q + scale, MSB plane + K
-    scale, V and O (fp16), plus the LSB plane for the refetched share."""
-    rows = B * H * seq
-    return rows * (D + 4 + D // 2 + 4 + 2 * D + 2 * D) + refetch_frac * rows * (D // 2) + B * seq * 4
+def make_peaked_inputs(seed, seq, torch, batch=B, alpha=PEAKED_ALPHA):
+    """A confident-attention input: K, V N(0,1) and q_i = alpha * k_i + N(0,1),
+    so every query's own key dominates its row (max probability well above
+    the refetch threshold): the op runs on the MSB plane alone."""
+    g = torch.Generator().manual_seed(seed)
+    k = torch.randn(batch, H, seq, D, generator=g)
+    v = torch.randn(batch, H, seq, D, generator=g)
+    q = alpha * k + torch.randn(batch, H, seq, D, generator=g)
+    return q.half(), k.half(), v.half()
 
 
-def algorithmic_work(seq, refetch_frac):
+def algorithmic_bytes(seq, refetch_frac, units=B * H, batch=B):
+    """Bytes one attention launch over ``units`` (batch, head) pairs must
+    move: int8 Q + scale, MSB plane + K scale, V and O (fp16), plus the LSB
+    plane for the refetched share, and the token importance."""
+    rows = units * seq
+    return rows * (D + 4 + D // 2 + 4 + 2 * D + 2 * D) + refetch_frac * rows * (D // 2) + batch * seq * 4
+
+
+def algorithmic_work(seq, refetch_frac, units=B * H):
     """Per launch: int8 ops of the scores (MSB score for every row, full score
     for the refetched rows), fp16 flops of P.V, and exp2 evaluations (MSB
     statistics, full statistics of the refetched rows, the final P)."""
-    units = B * H * seq * seq
-    return {"int8_ops": 2 * units * D * (1 + refetch_frac),
-            "f16_flops": 2 * units * D,
-            "exp2": units * (2 + refetch_frac)}
+    n = units * seq * seq
+    return {"int8_ops": 2 * n * D * (1 + refetch_frac),
+            "f16_flops": 2 * n * D,
+            "exp2": n * (2 + refetch_frac)}
 
 
 def measure_peaks(torch, dev):
@@ -254,26 +283,84 @@ def reference_bert_cpu(torch, runs=10):
     return ts[len(ts) // 2] * 1e3
 
 
-def ours_bert_b1(torch, dev, runs=10):
-    """The same B1 S128 fp32 forward through the patched model on the GPU."""
-    import copy
-    from spatten_b200.bert import patch_bert
-    model, ids, mask = bert_cpu_inputs(torch)
-    m = patch_bert(copy.deepcopy(model).to(dev).eval(), **BERT_CPU_KNOBS)
-    ids, mask = ids.to(dev), mask.to(dev)
+def graph_timed(torch, dev, fwd, steps, world=1):
+    """Time ``fwd`` (a forward returning a tensor): eagerly, and replayed as
+    one CUDA graph captured on a side stream, whose output must equal the
+    eager output bit for bit. With several ranks every rank replays its graph
+    (and the collectives inside it) or none does. Returns (ms per forward --
+    the graph's if it was captured --, launch kind, eager ms, error)."""
+    import torch.distributed as dist
     st = torch.cuda.current_stream(dev)
-    with torch.no_grad():
-        for _ in range(3):
-            m(input_ids=ids, attention_mask=mask)
-        torch.cuda.synchronize(dev)
+
+    def timed(fn):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(st)
-        for _ in range(runs):
-            m(input_ids=ids, attention_mask=mask)
+        for _ in range(steps):
+            fn()
         e1.record(st)
         torch.cuda.synchronize(dev)
-    return e0.elapsed_time(e1) / runs
+        return e0.elapsed_time(e1) / steps
+
+    def agree(flag):
+        if world == 1:
+            return flag
+        f = torch.tensor([1.0 if flag else 0.0], device=dev)
+        dist.all_reduce(f, op=dist.ReduceOp.MIN)
+        return bool(f.item() > 0)
+
+    with torch.no_grad():
+        for _ in range(2):
+            ref = fwd()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        eager_ms = timed(fwd)
+        graph_ms, err, g = None, None, None
+        try:
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(st)
+            with torch.cuda.stream(side):
+                fwd()
+            st.wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                out_g = fwd()
+        except RuntimeError as e:
+            g, err = None, str(e).splitlines()[0][:200]
+        if agree(g is not None):
+            g.replay()
+            torch.cuda.synchronize(dev)
+            if agree(torch.equal(out_g, ref)):
+                graph_ms = timed(g.replay)
+            else:
+                err = "graph output differs from the eager forward"
+        elif err is None:
+            err = "graph capture failed on another rank"
+        del g
+        torch.cuda.synchronize(dev)
+    ms = eager_ms if graph_ms is None else graph_ms
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, ("cuda_graph" if graph_ms is not None else "eager"), eager_ms, err
+
+
+def ours_bert_b1(torch, dev, steps=10):
+    """The same B1 S128 fp32 forward through the patched model on the GPU,
+    replayed as one CUDA graph (no padding, so no mask: HF's mask builders
+    test an all-ones mask on the host, which a graph cannot capture)."""
+    import copy
+    from transformers import BertConfig, BertModel
+    from spatten_b200.bert import patch_bert
+    torch.manual_seed(0)
+    model = BertModel(BertConfig(attn_implementation="sdpa")).eval()
+    _, ids, _ = bert_cpu_inputs(torch)
+    m = patch_bert(copy.deepcopy(model).to(dev).eval(), **BERT_CPU_KNOBS)
+    ids = ids.to(dev)
+    ms, kind, eager_ms, err = graph_timed(torch, dev, lambda: m(input_ids=ids).last_hidden_state, steps)
+    return {"ms_per_batch": ms, "launch": kind, "eager_ms_per_batch": eager_ms, "graph_error": err}
 
 
 def reference_arm(args, torch, rank, world):
@@ -286,9 +373,12 @@ def reference_arm(args, torch, rank, world):
     torch.set_num_threads(nthreads)
     heads = H
 
+    keep = max(1, math.ceil(TOKEN_KEEP * seq))
+
     def step(i):
         b = i % B
-        run_sample(q[b].float(), k[b].float(), v[b], SM_SCALE, REFETCH_THR, V_THR)
+        _, tok = run_sample(q[b].float(), k[b].float(), v[b], SM_SCALE, REFETCH_THR, V_THR)
+        torch.sort(torch.topk(tok, keep).indices)  # the cascade's token top-k
 
     for i in range(args.warmup):
         step(i)
@@ -300,8 +390,8 @@ def reference_arm(args, torch, rank, world):
     val = tokens / dt
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": config(seq),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": dict(config(seq), parallelism=f"{nthreads} host threads"),
             "cpu_baseline": {"value": val, "unit": UNIT, "cores": nthreads, "kind": "port",
                              "sample": f"one batch element (all {H} heads, S={seq}) per step, "
                                        "torch fp32 restatement of the op on the host cores"},
@@ -320,12 +410,12 @@ BERT_KNOBS = dict(enable_head_prune=True, head_keep_ratio=0.9, enable_token_prun
                   enable_prog_quant=True, quant_threshold=0.1)
 
 
-def bert_bench(torch, rank, world, dev, steps=5):
-    """BERT-base SpAtten forward, fp16, random-init weights (seed 0), batch 32
-    of random token ids at seq 512, token/head keep 0.9, V prune 1e-3,
-    progressive quantisation 0.1; the batch is sharded over the ranks and the
-    head importance all-reduced (batch-global head decisions). ms per global
-    batch = max over ranks."""
+def bert_model(torch, dev, seq, spatten=True, world=1):
+    """BERT-base (12 x 768, 12 heads, FFN 3072) random init from seed 0 in
+    fp16 on ``dev``; with ``spatten`` the attention modules are the drop-in's
+    with all knobs on. Positions beyond 512 need a larger position table
+    (the reference's seq-length benchmark raises max_position_embeddings the
+    same way)."""
     import torch.distributed as dist
     from transformers import BertConfig, BertModel
     from spatten_b200.bert import patch_bert
@@ -334,89 +424,56 @@ def bert_bench(torch, rank, world, dev, steps=5):
     # HF's mask builder, which for an unpadded batch passes no mask at all
     # (the "eager" builder materialises an additive [B, 1, S, S] zero mask
     # every forward, from a host-made scalar that graph capture rejects).
-    model = BertModel(BertConfig(attn_implementation="sdpa")).half().to(dev).eval()
-    knobs = dict(BERT_KNOBS)
-    if world > 1:
-        knobs["process_group"] = dist.group.WORLD
-    model = patch_bert(model, **knobs)
+    cfg = BertConfig(attn_implementation="sdpa", max_position_embeddings=max(512, seq))
+    model = BertModel(cfg).half().to(dev).eval()
+    if spatten:
+        knobs = dict(BERT_KNOBS)
+        if world > 1:
+            knobs["process_group"] = dist.group.WORLD
+        model = patch_bert(model, **knobs)
+    return model
+
+
+def bert_ids(torch, seq, rank=0, world=1):
     per = BERT_B // world
     g = torch.Generator().manual_seed(0)
-    ids = torch.randint(1000, 30522, (BERT_B, BERT_S), generator=g)[rank * per:(rank + 1) * per].to(dev)
+    return torch.randint(1000, 30522, (BERT_B, seq), generator=g)[rank * per:(rank + 1) * per]
+
+
+def bert_bench(torch, rank, world, dev, seq=BERT_S, steps=5, dense=False):
+    """BERT-base SpAtten forward, fp16, random-init weights (seed 0), batch 32
+    of random token ids at ``seq``, token/head keep 0.9, V prune 1e-3,
+    progressive quantisation 0.1; the batch is sharded over the ranks and the
+    head importance all-reduced (batch-global head decisions). ms per global
+    batch = max over ranks. With ``dense`` HF's own fp16 forward of the same
+    model (sdpa attention, no pruning) is timed beside it on one GPU."""
+    model = bert_model(torch, dev, seq, world=world)
+    ids = bert_ids(torch, seq, rank, world).to(dev)
     # no padding: no mask (an all-ones mask makes HF test it on the host every
     # forward, which a CUDA graph cannot capture)
-    mask = None
-    st = torch.cuda.current_stream(dev)
+    kept = {}
 
-    def timed(fn):
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        for _ in range(steps):
-            fn()
-        e1.record(st)
-        torch.cuda.synchronize(dev)
-        return e0.elapsed_time(e1) / steps
-
-    with torch.no_grad():
-        for _ in range(2):
-            ref = model(input_ids=ids, attention_mask=mask).last_hidden_state
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        eager_ms = timed(lambda: model(input_ids=ids, attention_mask=mask))
-        # The whole cascade forward as one CUDA graph (the kept token and
-        # head counts follow from the ratios, so every shape is static; the
-        # kept indices stay on the device). With several ranks the graph
-        # holds the per-layer head-importance all-reduce; every rank captures
-        # and replays the same number of times.
-        graph_ms = None
-        graph_error = None
-        g = None
-        try:
-            side = torch.cuda.Stream(dev)
-            side.wait_stream(st)
-            with torch.cuda.stream(side):
-                model(input_ids=ids, attention_mask=mask)
-            st.wait_stream(side)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                out_g = model(input_ids=ids, attention_mask=mask).last_hidden_state
-        except RuntimeError as err:
-            g = None
-            graph_error = str(err).splitlines()[0][:200]
-        ok = g is not None
-        if world > 1:  # every rank replays its graph (and its all-reduces), or none does
-            f = torch.tensor([1.0 if ok else 0.0], device=dev)
-            dist.all_reduce(f, op=dist.ReduceOp.MIN)
-            ok = bool(f.item() > 0)
-        if ok:
-            g.replay()
-            torch.cuda.synchronize(dev)
-            same = torch.equal(out_g, ref)
-            if world > 1:
-                f = torch.tensor([1.0 if same else 0.0], device=dev)
-                dist.all_reduce(f, op=dist.ReduceOp.MIN)
-                same = bool(f.item() > 0)
-            if same:
-                graph_ms = timed(g.replay)
-            else:
-                graph_error = "graph output differs from the eager forward"
-        elif graph_error is None:
-            graph_error = "graph capture failed on another rank"
-        del g
-        torch.cuda.synchronize(dev)
-    ms = eager_ms if graph_ms is None else graph_ms
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    return {"ms_per_batch": ms, "launch": "cuda_graph" if graph_ms is not None else "eager",
-            "graph_error": graph_error,
-            "eager_ms_per_batch": eager_ms, "batch": BERT_B, "seq_len": BERT_S, "per_rank_batch": per,
-            "dtype": "fp16", "steps": steps, "kept_tokens_last_layer": int(ref.shape[1]),
-            "config": "BERT-base (12x768, 12 heads, FFN 3072) random init seed 0, random ids, "
-                      "token/head keep 0.9, V prune 1e-3, progressive quant 0.1, batch sharded "
-                      "over ranks with head-importance all-reduce"}
+    def fwd():
+        out = model(input_ids=ids).last_hidden_state
+        kept["tokens"] = out.shape[1]
+        return out
+    ms, kind, eager_ms, err = graph_timed(torch, dev, fwd, steps, world)
+    del model
+    torch.cuda.empty_cache()
+    r = {"ms_per_batch": ms, "launch": kind, "graph_error": err, "eager_ms_per_batch": eager_ms,
+         "batch": BERT_B, "seq_len": seq, "per_rank_batch": BERT_B // world, "dtype": "fp16",
+         "steps": steps, "kept_tokens_last_layer": kept["tokens"],
+         "config": "BERT-base (12x768, 12 heads, FFN 3072) random init seed 0, random ids, "
+                   "token/head keep 0.9, V prune 1e-3, progressive quant 0.1, batch sharded "
+                   "over ranks with head-importance all-reduce"}
+    if dense:
+        hf = bert_model(torch, dev, seq, spatten=False)
+        ms_d, kind_d, _, _ = graph_timed(torch, dev, lambda: hf(input_ids=ids).last_hidden_state, steps)
+        del hf
+        torch.cuda.empty_cache()
+        r["dense_hf_sdpa_ms_per_batch"] = ms_d
+        r["dense_hf_launch"] = kind_d
+    return r
 
 
 QWEN3_B, QWEN3_S = 4, 8192
@@ -525,44 +582,142 @@ def decode_bench(torch, rank, world, dev, steps=3, batch=DEC_B):
                       "4-bit planes, importance all-reduced over KV-head shards, top-2048 per step"}
 
 
+class OpRunner:
+    """The op step on one rank's shard of the workload: quantise Q and K,
+    attention with V prune and importance, all-reduce of the partial token
+    importance over the head group (N > 1), cascade token top-k. Events
+    around the attention call and the all-reduce time them on the launching
+    stream."""
+
+    def __init__(self, torch, dev, seq, plan):
+        self.torch, self.dev, self.seq, self.plan = torch, dev, seq, plan
+        self.group = plan.groups() if plan is not None else None
+        self.keep = max(1, math.ceil(TOKEN_KEEP * seq))
+        self.st = torch.cuda.current_stream(dev)
+        self.ev = []
+
+    def step(self, q, k, v, record=False, want_refetch=False):
+        import spatten_b200 as sp
+        from spatten_b200._native import MODE_QUANT
+        from spatten_b200.distributed import allreduce_token_importance
+        torch = self.torch
+        q8, qs = sp.quant_q_int8(q)
+        kp = sp.quant_k_planes(k)
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
+        if record:
+            e[0].record(self.st)
+        r = sp.prog_attn(q8, kp.msb, v, k1=kp.lsb, mode=MODE_QUANT, q_scale=qs, k_scale=kp.scale,
+                         sm_scale=SM_SCALE, refetch_thr=REFETCH_THR, v_thr=V_THR, want_tok=True,
+                         want_head=True, want_refetch=want_refetch)
+        if record:
+            e[1].record(self.st)
+        tok = r.token_importance
+        if self.group is not None:
+            allreduce_token_importance(tok, self.group)
+        if record:
+            e[2].record(self.st)
+            self.ev.append(e)
+        kept = sp.topk_indices(tok, self.keep)
+        return r, kept
+
+    def times(self):
+        """(mean attention ms, mean all-reduce ms) of the recorded steps."""
+        attn = sum(a.elapsed_time(b) for a, b, _ in self.ev) / len(self.ev)
+        ar = sum(b.elapsed_time(c) for _, b, c in self.ev) / len(self.ev)
+        self.ev.clear()
+        return attn, ar
+
+
+def time_steps(torch, dev, fn, steps, barrier=None):
+    """Device time of ``steps`` calls of ``fn`` (CUDA events on the current
+    stream, synchronised and -- with ``barrier`` -- barriered on both sides)."""
+    st = torch.cuda.current_stream(dev)
+    if barrier:
+        barrier()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(st)
+    for _ in range(steps):
+        fn()
+    t1.record(st)
+    torch.cuda.synchronize(dev)
+    if barrier:
+        barrier()
+    return t0.elapsed_time(t1) / steps
+
+
+def roofline_of(seq, refetch_frac, attn_ms, peaks, measured, units=B * H, batch=B):
+    """Roofline of one attention launch (achieved tensor work against the
+    measured bf16 peak) and its time floor: the slowest of HBM bytes, int8 +
+    fp16 tensor work and MUFU exp2 at their measured rates."""
+    hbm_peak = float(measured.get("hbm_gbs", 6650.0))
+    tc_peak = float(measured.get("bf16_tflops", 1590.0))
+    peak_src = "measured" if measured else "fallback"
+    alg = algorithmic_bytes(seq, refetch_frac, units, batch)
+    work = algorithmic_work(seq, refetch_frac, units)
+    sec = attn_ms * 1e-3
+    hbm_gbs = alg / sec / 1e9
+    tensor_tflops = (work["int8_ops"] + work["f16_flops"]) / sec / 1e12
+    i8_rate = peaks.get("int8_ops_per_s") or 2 * tc_peak * 1e12
+    ex2_rate = peaks.get("exp2_per_s")
+    floors = {"hbm_ms": alg / (hbm_peak * 1e9) * 1e3,
+              "tensor_ms": (work["int8_ops"] / i8_rate + work["f16_flops"] / (tc_peak * 1e12)) * 1e3,
+              "mufu_ms": work["exp2"] / ex2_rate * 1e3 if ex2_rate else None}
+    limiter = max((k for k in floors if floors[k] is not None), key=lambda k: floors[k])
+    t_bound = floors[limiter]
+    return {"bound": "tensor", "achieved": tensor_tflops, "peak": tc_peak, "unit": "TFLOP/s",
+            "frac": tensor_tflops / tc_peak, "peak_source": f"{peak_src} (bf16 burst)",
+            "work_per_launch": work, "algorithmic_bytes": alg,
+            "hbm": {"achieved_gbs": hbm_gbs, "peak_gbs": hbm_peak, "frac": hbm_gbs / hbm_peak},
+            "t_bound": dict(floors, limiter=limiter.replace("_ms", ""), bound_ms=t_bound,
+                            frac=t_bound / attn_ms, int8_ops_per_s=i8_rate, exp2_per_s=ex2_rate)}
+
+
+def op_point(torch, dev, q, k, v, steps, peaks, measured, seq):
+    """One-GPU measurement of the op step on device-resident inputs: step
+    time, attention launch time, refetched share, roofline summary."""
+    run = OpRunner(torch, dev, seq, None)
+    for _ in range(3):
+        run.step(q, k, v)
+    r, _ = run.step(q, k, v, want_refetch=True)
+    refetch = float(r.refetch.float().mean())
+    del r
+    ms = time_steps(torch, dev, lambda: run.step(q, k, v, record=True), steps)
+    attn_ms, _ = run.times()
+    rl = roofline_of(seq, refetch, attn_ms, peaks, measured)
+    return {"seq_len": seq, "ms_per_step": ms, "attn_ms": attn_ms, "tokens_per_s": B * seq / (ms * 1e-3),
+            "refetch_fraction": refetch, "hbm_gbs": rl["hbm"]["achieved_gbs"],
+            "tensor_frac": rl["frac"], "t_bound_frac": rl["t_bound"]["frac"],
+            "t_bound_limiter": rl["t_bound"]["limiter"]}
+
+
 def ours_arm(args, torch, rank, world, local_rank):
     import torch.distributed as dist
     import spatten_b200 as sp
-    from spatten_b200._native import MODE_QUANT
+    from spatten_b200.distributed import HeadBatchShards, allreduce_token_importance
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     seq = args.seq
-    qh, kh, vh = make_inputs(SEED + rank, seq, torch)
-    qh, kh, vh = (t.pin_memory() for t in (qh, kh, vh))
+    plan = HeadBatchShards(B, H, rank, world)
+    units = (plan.b1 - plan.b0) * (plan.h1 - plan.h0)
+    qa, ka, va = make_inputs(SEED, seq, torch)
+    qh, kh, vh = (plan.take(t).contiguous().pin_memory() for t in (qa, ka, va))
+    del qa, ka, va
     q, k, v = (t.to(dev) for t in (qh, kh, vh))
     st = torch.cuda.current_stream(dev)
-
-    def step(q, k, v):
-        q8, qs = sp.quant_q_int8(q)
-        kp = sp.quant_k_planes(k)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        r = sp.prog_attn(q8, kp.msb, v, k1=kp.lsb, mode=MODE_QUANT, q_scale=qs, k_scale=kp.scale,
-                         sm_scale=SM_SCALE, refetch_thr=REFETCH_THR, v_thr=V_THR, want_tok=True,
-                         want_head=True)
-        e1.record(st)
-        return r, (e0, e1)
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
+    run = OpRunner(torch, dev, seq, plan)
     for _ in range(max(3, args.warmup)):
-        step(q, k, v)
+        run.step(q, k, v)
     torch.cuda.synchronize(dev)
-    # refetched share of rows, for the algorithmic LSB bytes
-    q8, qs = sp.quant_q_int8(q)
-    kp = sp.quant_k_planes(k)
-    r = sp.prog_attn(q8, kp.msb, v, k1=kp.lsb, mode=MODE_QUANT, q_scale=qs, k_scale=kp.scale,
-                     sm_scale=SM_SCALE, refetch_thr=REFETCH_THR, v_thr=V_THR, want_refetch=True)
+    r, _ = run.step(q, k, v, want_refetch=True)
     refetch_frac = float(r.refetch.float().mean())
-    del q8, qs, kp, r
+    del r
 
     peaks = measure_peaks(torch, dev) if rank == 0 else {}
     torch.cuda.synchronize(dev)
@@ -570,29 +725,19 @@ def ours_arm(args, torch, rank, world, local_rank):
     sampler = ClockSampler(visible_gpu_index(local_rank))
     sampler.start()
     time.sleep(0.5)
-    barrier()
-    torch.cuda.synchronize(dev)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    ev = []
-    t0.record(st)
-    for _ in range(args.steps):
-        _, e = step(q, k, v)
-        ev.append(e)
-    t1.record(st)
-    torch.cuda.synchronize(dev)
-    barrier()
+    ms = time_steps(torch, dev, lambda: run.step(q, k, v, record=True), args.steps, barrier)
     clocks = sampler.stop()
-    ms = t0.elapsed_time(t1) / args.steps
-    attn_ms = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+    attn_ms, ar_ms = run.times()
 
-    # End to end through the public API: every step copies its inputs from
-    # pinned host memory and its results back to pinned host memory. Copies
-    # run on their own streams so that step i+1's upload and step i-1's
-    # download overlap step i's compute (two device input buffers).
-    out_h = torch.empty((B, H, seq, D), dtype=torch.float16).pin_memory()
-    tok_h = torch.empty((B, seq), dtype=torch.float32).pin_memory()
-    head_h = torch.empty((H,), dtype=torch.float32).pin_memory()
+    # End to end through the public API: every step copies its shard's inputs
+    # from pinned host memory and its results (output, kept token indices)
+    # back to pinned host memory. Copies run on their own streams so that
+    # step i+1's upload and step i-1's download overlap step i's compute (two
+    # device input buffers).
+    Bl, Hl = plan.b1 - plan.b0, plan.h1 - plan.h0
+    out_h = torch.empty((Bl, Hl, seq, D), dtype=torch.float16).pin_memory()
+    kept_h = torch.empty((Bl, run.keep), dtype=torch.int64).pin_memory()
+    head_h = torch.empty((Hl,), dtype=torch.float32).pin_memory()
     up = torch.cuda.Stream(dev)
     down = torch.cuda.Stream(dev)
     dbuf = [[torch.empty_like(t, device=dev) for t in (qh, kh, vh)] for _ in range(2)]
@@ -600,6 +745,7 @@ def ours_arm(args, torch, rank, world, local_rank):
     loaded = [torch.cuda.Event() for _ in range(2)]   # upload into a buffer done
     done = torch.cuda.Event()                         # last download done
     keep = []
+    group = plan.groups()
 
     def e2e_steps(n):
         for i in range(n):
@@ -614,15 +760,19 @@ def ours_arm(args, torch, rank, world, local_rank):
             res = sp.progressive_attention(*dbuf[j], refetch_threshold=REFETCH_THR,
                                            v_prune_threshold=V_THR, sm_scale=SM_SCALE,
                                            return_importance=True)
+            tok = res.token_importance
+            if group is not None:
+                allreduce_token_importance(tok, group)
+            kept = sp.topk_indices(tok, run.keep)
             free[j].record(st)
             down.wait_stream(st)
             with torch.cuda.stream(down):
                 out_h.copy_(res.out, non_blocking=True)
-                tok_h.copy_(res.token_importance, non_blocking=True)
+                kept_h.copy_(kept, non_blocking=True)
                 head_h.copy_(res.head_abs_sum, non_blocking=True)
-                for t in (res.out, res.token_importance, res.head_abs_sum):
+                for t in (res.out, kept, res.head_abs_sum):
                     t.record_stream(down)
-            keep.append(res)
+            keep.append((res, kept))
             del keep[:-2]
         done.record(down)
         st.wait_event(done)
@@ -630,85 +780,89 @@ def ours_arm(args, torch, rank, world, local_rank):
 
     e2e_steps(2)
     torch.cuda.synchronize(dev)
-    barrier()
-    a0 = torch.cuda.Event(enable_timing=True)
-    a1 = torch.cuda.Event(enable_timing=True)
-    a0.record(st)
     up.wait_stream(st)
-    e2e_steps(args.steps)
-    a1.record(st)
-    torch.cuda.synchronize(dev)
-    barrier()
-    e2e_ms = a0.elapsed_time(a1) / args.steps
+    e2e_ms = time_steps(torch, dev, lambda: e2e_steps(args.steps), 1, barrier) / args.steps
     keep.clear()
+    del dbuf
 
-    dec = None if args.no_decode else decode_bench(torch, rank, world, dev)
-    bert = None
-    if not args.no_bert:
-        bert = bert_bench(torch, rank, world, dev)
-        if rank == 0:
-            bert["b1_s128_fp32_ms"] = ours_bert_b1(torch, dev)
-
-    if world > 1:
-        t = torch.tensor([ms, attn_ms, e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, attn_ms, e2e_ms = (float(x) for x in t.tolist())
-    if rank != 0:
-        return
-    tokens = B * seq * world
-    alg = algorithmic_bytes(seq, refetch_frac)
-    work = algorithmic_work(seq, refetch_frac)
     measured = {}
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(peaks_path):
         with open(peaks_path) as f:
             measured = json.load(f)
-    hbm_peak = float(measured.get("hbm_gbs", 6650.0))
-    tc_peak = float(measured.get("bf16_tflops", 1590.0))
-    peak_src = "measured" if measured else "fallback"
-    sec = attn_ms * 1e-3
-    hbm_gbs = alg / sec / 1e9
-    tensor_tflops = (work["int8_ops"] + work["f16_flops"]) / sec / 1e12
+
+    # one-GPU measurements on rank 0: the sequence sweep and the peaked input
+    sweep, peaked = None, None
+    if world == 1 and not args.no_sweep:
+        sweep = []
+        for s2 in SWEEP_SEQS:
+            if s2 == seq:
+                rl = roofline_of(seq, refetch_frac, attn_ms, peaks, measured)
+                sweep.append({"seq_len": seq, "ms_per_step": ms, "attn_ms": attn_ms,
+                              "tokens_per_s": B * seq / (ms * 1e-3), "refetch_fraction": refetch_frac,
+                              "hbm_gbs": rl["hbm"]["achieved_gbs"], "tensor_frac": rl["frac"],
+                              "t_bound_frac": rl["t_bound"]["frac"],
+                              "t_bound_limiter": rl["t_bound"]["limiter"]})
+                continue
+            qs_, ks_, vs_ = (t.to(dev) for t in make_inputs(SEED, s2, torch))
+            sweep.append(op_point(torch, dev, qs_, ks_, vs_, max(3, args.steps // 2), peaks, measured, s2))
+            del qs_, ks_, vs_
+        qp, kp_, vp = (t.to(dev) for t in make_peaked_inputs(SEED, seq, torch))
+        peaked = op_point(torch, dev, qp, kp_, vp, args.steps, peaks, measured, seq)
+        peaked["input"] = (f"K, V N(0,1), q_i = {PEAKED_ALPHA} * k_i + N(0,1) (each query's own key "
+                           "dominates its row)")
+        del qp, kp_, vp
+        torch.cuda.empty_cache()
+
+    dec = None if args.no_decode else decode_bench(torch, rank, world, dev)
+    bert = None
+    if not args.no_bert:
+        bert = bert_bench(torch, rank, world, dev, dense=(world == 1))
+        if world == 1:
+            bert["seq_sweep"] = [bert_bench(torch, 0, 1, dev, seq=s2, steps=3, dense=True)
+                                 for s2 in (2048, 4096)]
+            bert["b1_s128_fp32"] = ours_bert_b1(torch, dev)
+
+    t = torch.tensor([ms, attn_ms, e2e_ms, ar_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, attn_ms, e2e_ms, ar_ms = (float(x) for x in t.tolist())
+    if rank != 0:
+        return
+    tokens = B * seq
+    rl = roofline_of(seq, refetch_frac, attn_ms, peaks, measured, units, plan.b1 - plan.b0)
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "prog_attn_traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
             tr = json.load(f)
-        if tr.get("seq_len") == seq:
+        if tr.get("seq_len") == seq and tr.get("units", B * H) == units:
             traffic = tr.get("dram_bytes_per_launch")
-    # The time floor of the launch: the slowest of HBM bytes, tensor work
-    # (int8 and fp16 at their measured rates) and exp2 on the MUFU.
-    i8_rate = peaks.get("int8_ops_per_s") or 2 * tc_peak * 1e12
-    ex2_rate = peaks.get("exp2_per_s")
-    floors = {"hbm_ms": alg / (hbm_peak * 1e9) * 1e3,
-              "tensor_ms": (work["int8_ops"] / i8_rate + work["f16_flops"] / (tc_peak * 1e12)) * 1e3,
-              "mufu_ms": work["exp2"] / ex2_rate * 1e3 if ex2_rate else None}
-    limiter = max((k for k in floors if floors[k] is not None), key=lambda k: floors[k])
-    t_bound = floors[limiter]
+    rl["traffic"] = traffic
     line = {
         "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "s8 scores / f32 softmax / f16 P.V", "data": "synthetic", "config": config(seq),
-        "hbm_gbs": hbm_gbs, "attn_ms": attn_ms, "refetch_fraction": refetch_frac,
-        "roofline": {"bound": "tensor", "achieved": tensor_tflops, "peak": tc_peak, "unit": "TFLOP/s",
-                     "frac": tensor_tflops / tc_peak, "traffic": traffic,
-                     "peak_source": f"{peak_src} (bf16 burst)",
-                     "work_per_launch": work, "algorithmic_bytes": alg,
-                     "hbm": {"achieved_gbs": hbm_gbs, "peak_gbs": hbm_peak, "frac": hbm_gbs / hbm_peak},
-                     "t_bound": dict(floors, limiter=limiter.replace("_ms", ""), bound_ms=t_bound,
-                                     frac=t_bound / attn_ms,
-                                     int8_ops_per_s=i8_rate, exp2_per_s=ex2_rate)},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "s8 scores / f32 softmax / f16 P.V", "data": "synthetic", "config": config(seq, plan),
+        "hbm_gbs": rl["hbm"]["achieved_gbs"], "attn_ms": attn_ms, "refetch_fraction": refetch_frac,
+        "units_per_rank": units, "allreduce_ms": ar_ms if world > 1 else 0.0,
+        "roofline": rl,
         "clocks": clocks,
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": 3 * B * H * seq * D * 2,
-                "d2h_bytes_per_step": B * H * seq * D * 2 + B * seq * 4 + H * 4},
+                # outputs, and every rank's copy of its batch rows' kept indices and its head sums
+                "d2h_bytes_per_step": B * H * seq * D * 2 + plan.head_ranks * B * run.keep * 8
+                + H * 4 * plan.batch_ranks},
     }
+    if sweep is not None:
+        line["seq_sweep"] = sweep
+        line["peaked"] = peaked
     if bert is not None:
         line["bert"] = bert
     if dec is not None:
         hbm = dec["hbm_gbs_per_gpu"]
+        hbm_peak = rl["hbm"]["peak_gbs"]
         dec["roofline"] = {"bound": "hbm", "achieved": hbm, "peak": hbm_peak, "unit": "GB/s",
                            "frac": hbm / hbm_peak}
         line["qwen3_decode"] = dec
@@ -716,11 +870,10 @@ def ours_arm(args, torch, rank, world, local_rank):
         line["qwen3_prefill"] = qwen3_bench(torch, dev)
     if world == 1 and not args.no_cpu_baseline:
         qc, kc, vc = (t.cpu() for t in (qh, kh, vh))
-        hs = H
-        dt = cpu_sample(torch, qc, kc, vc, hs)
-        line["cpu_baseline"] = {"value": seq * hs / H / dt, "unit": UNIT,
+        dt = cpu_sample(torch, qc, kc, vc, H)
+        line["cpu_baseline"] = {"value": seq * H / H / dt, "unit": UNIT,
                                 "cores": os.cpu_count() or 1, "kind": "port",
-                                "sample": f"one batch element, {hs} heads, S={seq}: torch fp32 "
+                                "sample": f"one batch element, {H} heads, S={seq}: torch fp32 "
                                           "restatement of the op on all host cores"}
     print(json.dumps(line), flush=True)
 

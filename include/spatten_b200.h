@@ -144,6 +144,11 @@ typedef struct spatten_prog_attn_args {
                                keys n < key_limit[z*M + m] only (the causal mask of a
                                position-sorted subset of keys, e.g. a pruned KV cache);
                                replaces `causal` when set. (ABI version 3) */
+  int score_row_stride; /* with score_out: write the scores of rows m % score_row_stride == 0
+                           only, row m at row m / score_row_stride of a
+                           [Z, H, ceil(M / score_row_stride), N] array (0 or 1: every row),
+                           so a full-size launch can be verified from a sample of its rows
+                           without a [Z, H, M, N] dump. (ABI version 4) */
 } spatten_prog_attn_args;
 
 /* Bytes of workspace spatten_prog_attn needs for these arguments (0 if no

@@ -117,6 +117,79 @@ def _finish(p, vv, v_thr, s=None, v_count=0):
     return pp, out, cgap
 
 
+def quant_head(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.0, bias=None,
+               excl=None, band=1e-4, v_count=0, return_scores=False, decisions_only=False,
+               chunk=1024):
+    """One (batch, head) of :func:`prog_attn_quant`, over the query rows in
+    chunks of ``chunk`` (every step is row-wise except the column sums of the
+    token importance, which add up over the chunks), so that full-size heads
+    fit in memory and heads can run on several threads.
+
+    q8 [M, D] int8, sq [M], msb_p / lsb_p [N, D/2] packed planes, sk [N],
+    v [N, D] (unused with ``decisions_only``), bias [M, N] or None, excl
+    [M, N] bool (keys a row does not see) or None. With ``decisions_only``
+    only the refetch decisions and the MSB max-probabilities are computed
+    (pass 1 of the op)."""
+    from .quant import unpack_nibbles
+    q8 = np.asarray(q8, np.int8)
+    M = q8.shape[0]
+    msb = unpack_nibbles(msb_p, signed=True).astype(np.int16)
+    k16 = (16 * msb).astype(np.int8)
+    k8 = None
+    if not decisions_only:
+        lsb = unpack_nibbles(lsb_p, signed=False).astype(np.int16)
+        k8 = (16 * msb + lsb).astype(np.int8)
+    N = k16.shape[0]
+    skf = np.asarray(sk, np.float32)
+    refetch = np.zeros(M, bool)
+    maxprob = np.zeros(M)
+    res = dict(refetch=refetch, maxprob=maxprob)
+    if not decisions_only:
+        out = np.zeros((M, q8.shape[1]))
+        tok = np.zeros(N)
+        amb = np.zeros(N)
+        res.update(out=out, tok=tok, amb=amb, head_abs=0.0, pgap=np.inf, cgap=np.inf)
+        if return_scores:
+            res["A"] = np.zeros((M, N), np.int32)
+            res["F"] = np.zeros((M, N), np.int32)
+    for r0 in range(0, M, chunk):
+        rows = slice(r0, min(M, r0 + chunk))
+        ex = excl[rows] if excl is not None else None
+        A = int_scores(q8[rows], k16)
+        c = (np.asarray(sq[rows], np.float32) * np.float32(sm_scale)).astype(np.float32)
+        cs = (c[:, None] * skf[None, :]).astype(np.float32)
+        s_msb = (A.astype(np.float32) * cs).astype(np.float32)
+        if bias is not None:
+            s_msb = (s_msb + bias[rows]).astype(np.float32)
+        _, _, l1 = _softmax_rows(s_msb, ex)
+        with np.errstate(divide="ignore"):  # a row that sees no key: l = 0
+            mp = 1.0 / l1
+        rf = mp < refetch_thr
+        refetch[rows] = rf
+        maxprob[rows] = mp
+        if decisions_only:
+            continue
+        F = int_scores(q8[rows], k8)
+        s_full = (F.astype(np.float32) * cs).astype(np.float32)
+        if bias is not None:
+            s_full = (s_full + bias[rows]).astype(np.float32)
+        s = np.where(rf[:, None], s_full, s_msb)
+        p, _, _ = _softmax_rows(s, ex)
+        if v_thr > 0:
+            res["pgap"] = min(res["pgap"], np.min(np.abs(p - v_thr)) / v_thr)
+            amb += (np.abs(p - v_thr) < band * v_thr).sum(axis=0)
+        s_ord = np.where(ex, -np.inf, s) if ex is not None else s
+        pp, o, g = _finish(p, np.asarray(v), v_thr, s_ord, v_count)
+        res["cgap"] = min(res["cgap"], g)
+        out[rows] = o
+        tok += pp.sum(axis=0)
+        res["head_abs"] += np.abs(o).sum()
+        if return_scores:
+            res["A"][rows] = A
+            res["F"][rows] = F
+    return res
+
+
 def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.0,
                     bias=None, causal=False, return_scores=False, band=1e-4, v_count=0,
                     key_limit=None):
@@ -125,7 +198,6 @@ def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.
     v [Z,Hkv,N,D]. ``v_count`` > 0 applies the reference's count V prune (on
     top of ``v_thr``). ``key_limit`` [Z, M]: row m sees keys n < key_limit[z, m]
     (replaces ``causal``). Returns a dict of float64 outputs and diagnostics."""
-    from .quant import unpack_nibbles
     q8 = np.asarray(q8, np.int8)
     Z, H, M, D = q8.shape
     Hkv, N = msb_p.shape[1], msb_p.shape[2]
@@ -143,40 +215,19 @@ def prog_attn_quant(q8, sq, msb_p, lsb_p, sk, v, sm_scale, refetch_thr, v_thr=0.
         excl = _limit_mask(key_limit[z], N) if key_limit is not None else excl0
         for h in range(H):
             kh = _kv_head(h, H, Hkv)
-            msb = unpack_nibbles(msb_p[z, kh], signed=True).astype(np.int16)
-            lsb = unpack_nibbles(lsb_p[z, kh], signed=False).astype(np.int16)
-            k16 = (16 * msb).astype(np.int8)
-            k8 = (16 * msb + lsb).astype(np.int8)
-            A = int_scores(q8[z, h], k16)
-            F = int_scores(q8[z, h], k8)
-            c = (np.asarray(sq[z, h], np.float32) * np.float32(sm_scale)).astype(np.float32)
-            cs = (c[:, None] * np.asarray(sk[z, kh], np.float32)[None, :]).astype(np.float32)
-            bb = _bias_for(bias, z, h, M, N)
-            s_msb = (A.astype(np.float32) * cs).astype(np.float32)
-            s_full = (F.astype(np.float32) * cs).astype(np.float32)
-            if bb is not None:
-                s_msb = (s_msb + bb).astype(np.float32)
-                s_full = (s_full + bb).astype(np.float32)
-            _, _, l1 = _softmax_rows(s_msb, excl)
-            with np.errstate(divide="ignore"):  # a row that sees no key: l = 0
-                mp = 1.0 / l1
-            rf = mp < refetch_thr
-            s = np.where(rf[:, None], s_full, s_msb)
-            p, _, _ = _softmax_rows(s, excl)
-            if v_thr > 0:
-                gap = np.min(np.abs(p - v_thr)) / v_thr
-                pgap = min(pgap, gap)
-                amb[z] += (np.abs(p - v_thr) < band * v_thr).sum(axis=0)
-            s_ord = np.where(excl, -np.inf, s) if excl is not None else s
-            pp, o, g = _finish(p, np.asarray(v[z, kh]), v_thr, s_ord, v_count)
-            cgap = min(cgap, g)
-            out[z, h] = o
-            refetch[z, h] = rf
-            maxprob[z, h] = mp
-            tok_h[z, h] = pp.sum(axis=0)
-            head_abs[z, h] = np.abs(o).sum()
+            r = quant_head(q8[z, h], sq[z, h], msb_p[z, kh], lsb_p[z, kh], sk[z, kh], v[z, kh],
+                           sm_scale, refetch_thr, v_thr, bias=_bias_for(bias, z, h, M, N),
+                           excl=excl, band=band, v_count=v_count, return_scores=return_scores)
+            pgap = min(pgap, r["pgap"])
+            cgap = min(cgap, r["cgap"])
+            amb[z] += r["amb"]
+            out[z, h] = r["out"]
+            refetch[z, h] = r["refetch"]
+            maxprob[z, h] = r["maxprob"]
+            tok_h[z, h] = r["tok"]
+            head_abs[z, h] = r["head_abs"]
             if return_scores:
-                scores[(z, h)] = (A, F)
+                scores[(z, h)] = (r["A"], r["F"])
     res = dict(out=out, refetch=refetch, maxprob_msb=maxprob, tok_per_head=tok_h,
                tok=tok_h.sum(axis=1), head_abs=head_abs, vprune_gap=pgap, vprune_amb=amb,
                vcount_gap=cgap, refetch_gap=np.min(np.abs(maxprob - refetch_thr)) / max(abs(refetch_thr), 1e-30))

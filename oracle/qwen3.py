@@ -50,33 +50,13 @@ def spatten_qwen3_forward(model, input_ids, enable_token_prune=False, token_keep
     for layer in base.layers:
         a = layer.self_attn
         h = layer.input_layernorm(x)
-        q = a.q_norm(a.q_proj(h).view(B, S, H, d))
-        k = a.k_norm(a.k_proj(h).view(B, S, Hkv, d))
-        v = a.v_proj(h).view(B, S, Hkv, d)
-        q, k = apply_rotary_pos_emb(q, k, cos, sin, unsqueeze_dim=2)
         K = pos.shape[1]
-        kk = np.stack([k[b].numpy()[pos[b]] for b in range(B)])  # [B, K, Hkv, d]
-        vv = np.stack([v[b].numpy()[pos[b]] for b in range(B)])
-        lim = np.stack([np.searchsorted(pos[b], np.arange(S), side="right") for b in range(B)])
-        qh = q.permute(0, 2, 1, 3).numpy()
-        kh = np.ascontiguousarray(kk.transpose(0, 2, 1, 3))
-        vh = np.ascontiguousarray(vv.transpose(0, 2, 1, 3))
-        v_thr, v_count = 0.0, 0
-        if enable_v_prune:
-            if v_prune_threshold is not None:
-                v_thr = float(v_prune_threshold)
-            elif v_prune_num > 0 and K > v_prune_num:
-                v_count = int(v_prune_num)
+        r, o = attention_layer(a, h, cos, sin, pos, enable_v_prune=enable_v_prune,
+                               v_prune_threshold=v_prune_threshold, v_prune_num=v_prune_num,
+                               enable_prog_quant=enable_prog_quant, quant_threshold=quant_threshold)
         if enable_prog_quant:
-            q8, sq = quant_rows_int8(qh)
-            msb, lsb, sk = quant_k_planes(kh)
-            r = prog_attn_quant(q8, sq, msb, lsb, sk, vh, a.scaling, quant_threshold, v_thr,
-                                key_limit=lim, v_count=v_count)
             rec["refetch"].append(r["refetch"])
             rec["refetch_gap"] = min(rec["refetch_gap"], r["refetch_gap"])
-        else:
-            r = prog_attn_dense(qh, kh, vh, a.scaling, v_thr, key_limit=lim, v_count=v_count)
-        o = torch.from_numpy(r["out"].astype(np.float32)).permute(0, 2, 1, 3).reshape(B, S, H * d)
         x = x + a.o_proj(o)
         x = x + layer.mlp(layer.post_attention_layernorm(x))
         tok = r["tok"] if cum is None else r["tok"] + cum
@@ -100,3 +80,42 @@ def spatten_qwen3_forward(model, input_ids, enable_token_prune=False, token_keep
             cum = tok
     rec["last_hidden_state"] = base.norm(x)
     return rec
+
+
+@torch.no_grad()
+def attention_layer(a, h, cos, sin, pos, enable_v_prune=False, v_prune_threshold=None,
+                    v_prune_num=2, enable_prog_quant=False, quant_threshold=0.1):
+    """The SpAtten attention of one Qwen3 layer (module ``a``) on its
+    normalised input ``h`` [B, S, hidden] (fp32, CPU): Q/K/V projections,
+    QK-norm, RoPE (cos / sin [B, S, D]), attention of every query position
+    over the kept keys at positions ``pos`` [B, K] (ascending), causal by
+    position. Returns (the core's dict -- see oracle.prog_attn --, the
+    attention output [B, S, H * D] before ``o_proj``)."""
+    B, S, _ = h.shape
+    H, Hkv, d = a.config.num_attention_heads, a.config.num_key_value_heads, a.head_dim
+    q = a.q_norm(a.q_proj(h).view(B, S, H, d))
+    k = a.k_norm(a.k_proj(h).view(B, S, Hkv, d))
+    v = a.v_proj(h).view(B, S, Hkv, d)
+    q, k = apply_rotary_pos_emb(q, k, cos, sin, unsqueeze_dim=2)
+    K = pos.shape[1]
+    kk = np.stack([k[b].numpy()[pos[b]] for b in range(B)])  # [B, K, Hkv, d]
+    vv = np.stack([v[b].numpy()[pos[b]] for b in range(B)])
+    lim = np.stack([np.searchsorted(pos[b], np.arange(S), side="right") for b in range(B)])
+    qh = q.permute(0, 2, 1, 3).numpy()
+    kh = np.ascontiguousarray(kk.transpose(0, 2, 1, 3))
+    vh = np.ascontiguousarray(vv.transpose(0, 2, 1, 3))
+    v_thr, v_count = 0.0, 0
+    if enable_v_prune:
+        if v_prune_threshold is not None:
+            v_thr = float(v_prune_threshold)
+        elif v_prune_num > 0 and K > v_prune_num:
+            v_count = int(v_prune_num)
+    if enable_prog_quant:
+        q8, sq = quant_rows_int8(qh)
+        msb, lsb, sk = quant_k_planes(kh)
+        r = prog_attn_quant(q8, sq, msb, lsb, sk, vh, a.scaling, quant_threshold, v_thr,
+                            key_limit=lim, v_count=v_count)
+    else:
+        r = prog_attn_dense(qh, kh, vh, a.scaling, v_thr, key_limit=lim, v_count=v_count)
+    o = torch.from_numpy(r["out"].astype(np.float32)).permute(0, 2, 1, 3).reshape(B, S, H * d)
+    return r, o

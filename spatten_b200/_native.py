@@ -18,7 +18,7 @@ DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
 MODE_QUANT, MODE_DENSE, MODE_COMPAT = 0, 1, 2
 PROJ_QUANT, PROJ_DENSE = 0, 1
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 MAX_V_PRUNE_COUNT = 8  # spatten_prog_attn_args.v_prune_count limit
 
 c_i64 = ctypes.c_int64
@@ -44,6 +44,7 @@ class ProgAttnArgs(ctypes.Structure):
         ("tile_m", c_int), ("tile_n", c_int), ("tile_thr", c_float), ("causal", c_int),
         ("tok_out", c_vp), ("tok_in", c_vp), ("head_out", c_vp), ("refetch_out", c_vp),
         ("score_out", c_vp), ("v_prune_count", c_int), ("key_limit", c_vp),
+        ("score_row_stride", c_int),
     ]
 
 

@@ -78,7 +78,7 @@ int spatten::set_last_error(int code, const char* msg) {
 
 extern "C" {
 
-int spatten_abi_version(void) { return 3; }
+int spatten_abi_version(void) { return 4; }
 
 const char* spatten_last_error(void) { return g_err.c_str(); }
 
@@ -166,6 +166,7 @@ static int fill_params(const spatten_prog_attn_args* a, spatten::AttnParams& p) 
   if (a->key_limit && a->mode == SPATTEN_MODE_COMPAT)
     return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: COMPAT has no key_limit");
   if (a->key_limit && !aligned(a->key_limit, 4)) return fail(SPATTEN_ERR_INVALID, "prog_attn: key_limit not aligned");
+  if (a->score_row_stride < 0) return fail(SPATTEN_ERR_INVALID, "prog_attn: negative score_row_stride");
   p.mode = a->mode;
   p.dtype = a->dtype;
   p.Z = a->Z; p.H = a->H; p.Hkv = a->Hkv; p.M = a->M; p.N = a->N; p.D = a->D;
@@ -186,6 +187,7 @@ static int fill_params(const spatten_prog_attn_args* a, spatten::AttnParams& p) 
   if (a->key_limit) p.causal = 0;
   p.refetch_out = quant ? a->refetch_out : nullptr;
   p.score_out = quant ? a->score_out : nullptr;
+  p.score_rs = a->score_row_stride > 1 ? a->score_row_stride : 1;
   const int rows = spatten::attn_tile_rows(p);
   p.mtiles = (a->M + rows - 1) / rows;
   p.tok_partial = nullptr;

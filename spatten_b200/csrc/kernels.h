@@ -31,7 +31,8 @@ struct AttnParams {
   int v_count;          // count V prune: zero the v_count smallest p of each row (0: off)
   const int32_t* key_limit;  // [Z, M]: row m sees keys n < key_limit[z*M+m] (null: causal / all)
   uint8_t* refetch_out;
-  int32_t* score_out;
+  int32_t* score_out;   // [Z, H, ceil(M / score_rs), N]: rows m % score_rs == 0
+  int score_rs;
   // workspace (per-CTA partial sums, reduced by importance_reduce)
   int mtiles;           // query tiles per (z, h)
   float* tok_partial;   // [Z, H, mtiles, N] or null

@@ -599,9 +599,9 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
     __syncwarp();
     if (lane == 0) mbar_arrive(&b.s_empty[sb]);
     const int n0 = j * BN + c0;
-    if (dump && valid) {
+    if (dump && valid && row % p.score_rs == 0) {
       for (int i = 0; i < HC; ++i)
-        if (n0 + i < p.N) dump[(int64_t)row * p.N + n0 + i] = (int32_t)u[i];
+        if (n0 + i < p.N) dump[(int64_t)(row / p.score_rs) * p.N + n0 + i] = (int32_t)u[i];
     }
     if (!mbar_wait(&b.k_full[es], (tt / kNExp) & 1, kErrSoftmax | 2, abort)) { alive = false; return; }
     const float* ks = ksm + es * BN + c0;
@@ -729,7 +729,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
   int any = 0;
   const float vthr = p.v_thr;
   int32_t* dump = (MODE == kQuant && p.score_out)
-                      ? p.score_out + ((int64_t)z * p.H + h) * p.M * (int64_t)p.N
+                      ? p.score_out + ((int64_t)z * p.H + h) * ((p.M + p.score_rs - 1) / p.score_rs) * (int64_t)p.N
                       : nullptr;
   f2 inv2 = pack_f2(0.f, 0.f), mn2 = pack_f2(0.f, 0.f);
   // Count V prune (VC): this thread's kMaxVPruneCount smallest (score, key)

@@ -62,3 +62,46 @@ def allreduce_token_importance(tok, group=None):
     """Sum the per-rank partial token importance [B, S] (heads split across ranks)."""
     dist.all_reduce(tok, op=dist.ReduceOp.SUM, group=group)
     return tok
+
+
+class HeadBatchShards:
+    """Partition of a [B, H] grid of (batch, head) units over ``world`` ranks:
+    the heads are split over ``head_ranks`` ranks (the largest divisor of H
+    that divides ``world`` and is at most ``max_head_ranks``), the batch over
+    the remaining ``world // head_ranks``. Rank r holds heads
+    [h0, h1) of batch rows [b0, b1); the ranks that share its batch rows form
+    its head group, over which the token importance is all-reduced.
+    ``groups()`` must be called on every rank (it creates the process groups
+    in the same order everywhere)."""
+
+    def __init__(self, B, H, rank, world_size, max_head_ranks=4):
+        hr = 1
+        for c in range(1, min(max_head_ranks, world_size) + 1):
+            if H % c == 0 and world_size % c == 0:
+                hr = c
+        br = world_size // hr
+        if B % br:
+            raise ValueError(f"batch {B} does not split over {br} ranks")
+        self.B, self.H, self.rank, self.world = B, H, rank, world_size
+        self.head_ranks, self.batch_ranks = hr, br
+        hi, bi = rank % hr, rank // hr
+        self.h0, self.h1 = hi * H // hr, (hi + 1) * H // hr
+        self.b0, self.b1 = bi * B // br, (bi + 1) * B // br
+        self._group = None
+
+    def groups(self):
+        """This rank's head group (None with one head rank)."""
+        if self.head_ranks == 1:
+            return None
+        if self._group is None:
+            mine = None
+            for bi in range(self.batch_ranks):
+                g = dist.new_group([bi * self.head_ranks + i for i in range(self.head_ranks)])
+                if bi == self.rank // self.head_ranks:
+                    mine = g
+            self._group = mine
+        return self._group
+
+    def take(self, x):
+        """This rank's units of a [B, H, ...] tensor."""
+        return x[self.b0:self.b1, self.h0:self.h1]

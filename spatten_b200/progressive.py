@@ -73,7 +73,7 @@ class AttnResult(NamedTuple):
     token_importance: Optional[torch.Tensor]  # [Z, N] sum over heads, queries of pruned P
     head_abs_sum: Optional[torch.Tensor]      # [H] sum over (z, m, d) of |out|
     refetch: Optional[torch.Tensor]           # [Z, H, M] bool, QUANT only
-    scores: Optional[torch.Tensor] = None     # [Z, H, M, N] int32 scores used, QUANT only
+    scores: Optional[torch.Tensor] = None     # [Z, H, M / row stride, N] int32 scores used, QUANT only
 
 
 def quant_q_int8(x):
@@ -118,14 +118,17 @@ def _bias_view(bias, Z, H, M, Nk, device):
 def prog_attn(q, k0, v, *, mode, k1=None, q_scale=None, k_scale=None, sm_scale=None,
               refetch_thr=0.1, v_thr=0.0, bias=None, causal=False, tile=(32, 32), tile_thr=0.0,
               tok_in=None, want_tok=False, want_head=False, want_refetch=False, want_scores=False,
-              out=None, out_head_map=None, out_head_slots=0, v_prune_count=0, key_limit=None):
+              out=None, out_head_map=None, out_head_slots=0, v_prune_count=0, key_limit=None,
+              score_row_stride=1):
     """General progressive attention (see spatten_prog_attn_args in
     include/spatten_b200.h). ``q`` int8 for QUANT; ``k0``/``k1`` are the
     MSB/LSB planes (QUANT), k (DENSE) or k_msb/k_lsb (COMPAT).
     ``v_prune_count`` (0..8) zeroes that many smallest probabilities of
     every row longer than it (the reference's count V prune). ``key_limit``
     [Z, M] int: row m of batch z sees keys n < key_limit[z, m] only (causal
-    attention over a position-sorted subset of keys); replaces ``causal``."""
+    attention over a position-sorted subset of keys); replaces ``causal``.
+    ``want_scores`` returns the integer scores of rows m % score_row_stride
+    == 0 as [Z, H, ceil(M / score_row_stride), N] int32."""
     _cuda(q, k0, k1, v, q_scale, k_scale, bias, tok_in, out)
     q4, k04, v4 = _as4d(q, "q"), _as4d(k0, "k"), _as4d(v, "v")
     k14 = None if k1 is None else _as4d(k1, "k1")
@@ -178,7 +181,9 @@ def prog_attn(q, k0, v, *, mode, k1=None, q_scale=None, k_scale=None, sm_scale=N
     ref = torch.empty((Z, H, M), dtype=torch.uint8, device=v.device) if want_refetch else None
     if tok_in is not None:
         tok_in = tok_in.float().contiguous()
-    sco = torch.empty((Z, H, M, Nk), dtype=torch.int32, device=v.device) if want_scores else None
+    rs = max(1, int(score_row_stride))
+    sco = torch.empty((Z, H, -(-M // rs), Nk), dtype=torch.int32, device=v.device) if want_scores else None
+    a.score_row_stride = rs
     a.tok_out, a.tok_in, a.head_out, a.refetch_out = _ptr(tok), _ptr(tok_in), _ptr(head), _ptr(ref)
     a.score_out = _ptr(sco)
     ws_bytes = N.lib.spatten_prog_attn_workspace_size(a)

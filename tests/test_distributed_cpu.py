@@ -71,3 +71,52 @@ def test_gloo_two_ranks_importance_allreduce():
     expect = ctx.abs().sum(dim=(1, 3)).numpy()
     for _, _, tok, _ in out:
         np.testing.assert_allclose(tok, expect, rtol=1e-5)
+
+
+def test_head_batch_shards_partition():
+    """Every (batch, head) unit of the B8 H12 op workload lands on exactly one
+    rank; heads split over up to 4 ranks, the batch over the rest."""
+    from spatten_b200.distributed import HeadBatchShards
+    for world, (hr, br) in {1: (1, 1), 2: (2, 1), 4: (4, 1), 8: (4, 2)}.items():
+        seen = np.zeros((8, 12), int)
+        for r in range(world):
+            p = HeadBatchShards(8, 12, r, world)
+            assert (p.head_ranks, p.batch_ranks) == (hr, br)
+            seen[p.b0:p.b1, p.h0:p.h1] += 1
+        assert (seen == 1).all(), world
+
+
+def _head_group_worker(rank, world, port, x, q):
+    import torch.distributed as dist
+    from spatten_b200.distributed import HeadBatchShards, allreduce_token_importance
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        plan = HeadBatchShards(x.shape[0], x.shape[1], rank, world, max_head_ranks=2)
+        part = plan.take(x).sum(dim=1).contiguous()  # [B_local, S]: my heads' partial sums
+        tok = allreduce_token_importance(part, plan.groups())
+        q.put((rank, plan.b0, plan.b1, tok.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_four_ranks_head_group_allreduce():
+    """Four ranks as 2 head ranks x 2 batch ranks: each head group's
+    all-reduce gives the sum over all heads for its own batch rows only."""
+    g = torch.Generator().manual_seed(1)
+    x = torch.rand(4, 6, 9, generator=g)
+    world = 4
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    port = _free_port()
+    procs = [mpc.Process(target=_head_group_worker, args=(r, world, port, x, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    full = x.sum(dim=1).numpy()
+    for rank, b0, b1, tok in out:
+        np.testing.assert_allclose(tok, full[b0:b1], rtol=1e-6)
