@@ -60,7 +60,7 @@ extern "C" {
 
 #define SPATTEN_MODE_QUANT 0  /* int8 Q, 4-bit MSB/LSB K planes, row max-prob refetch */
 #define SPATTEN_MODE_DENSE 1  /* float Q/K (progressive quantisation off) */
-#define SPATTEN_MODE_COMPAT 2 /* float K planes with the reference's tile criterion */
+#define SPATTEN_MODE_COMPAT 2 /* float K planes with the reference's tile criterion (no mask) */
 
 /* ABI version; bumped on any incompatible change of this header. */
 int spatten_abi_version(void);
@@ -138,7 +138,7 @@ typedef struct spatten_prog_attn_args {
   int v_prune_count; /* count V prune (the reference's v_prune_num, spatten_bert.py:100-113):
                         in rows of more than v_prune_count keys, zero the v_prune_count
                         smallest probabilities (ties to the smaller key index), no
-                        renormalisation; 0 disables, at most 8; QUANT and DENSE only.
+                        renormalisation; 0 disables, at most 16; QUANT and DENSE only.
                         Applies together with v_thr. (ABI version 2) */
   const int32_t* key_limit; /* optional [Z, M] int32, QUANT and DENSE: row m of batch z sees
                                keys n < key_limit[z*M + m] only (the causal mask of a

@@ -19,7 +19,7 @@ MODE_QUANT, MODE_DENSE, MODE_COMPAT = 0, 1, 2
 PROJ_QUANT, PROJ_DENSE = 0, 1
 
 ABI_VERSION = 4
-MAX_V_PRUNE_COUNT = 8  # spatten_prog_attn_args.v_prune_count limit
+MAX_V_PRUNE_COUNT = 16  # spatten_prog_attn_args.v_prune_count limit
 
 c_i64 = ctypes.c_int64
 c_vp = ctypes.c_void_p

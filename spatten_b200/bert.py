@@ -24,7 +24,7 @@ Knobs (per attention module): ``enable_head_prune``/``head_prune_num``,
 and threshold knobs ``head_keep_ratio``, ``token_keep_ratio`` (keep
 ``max(1, ceil(ratio * current))``, overriding the count) and
 ``v_prune_threshold`` (zero ``p < thr``; used instead of the count when set;
-without it ``v_prune_num`` <= 8 zeroes that many smallest probabilities of
+without it ``v_prune_num`` <= 16 zeroes that many smallest probabilities of
 every row, ties to the smaller key index).
 ``quant_threshold`` is the row max-probability below which a row's LSB plane
 is refetched (the reference used it as a tile logit bound).

@@ -163,8 +163,8 @@ static int fill_params(const spatten_prog_attn_args* a, spatten::AttnParams& p) 
                 spatten::kMaxVPruneCount);
   if (a->v_prune_count > 0 && a->mode == SPATTEN_MODE_COMPAT)
     return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: COMPAT has no count V prune");
-  if (a->key_limit && a->mode == SPATTEN_MODE_COMPAT)
-    return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: COMPAT has no key_limit");
+  if ((a->key_limit || a->bias || a->causal) && a->mode == SPATTEN_MODE_COMPAT)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "prog_attn: COMPAT takes no mask (the reference op has none)");
   if (a->key_limit && !aligned(a->key_limit, 4)) return fail(SPATTEN_ERR_INVALID, "prog_attn: key_limit not aligned");
   if (a->score_row_stride < 0) return fail(SPATTEN_ERR_INVALID, "prog_attn: negative score_row_stride");
   p.mode = a->mode;

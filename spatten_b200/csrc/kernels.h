@@ -44,16 +44,14 @@ cudaError_t launch_quant(int dtype, bool planes, const void* x, int Z, int H, in
                          uint8_t* lsb, float* scale, cudaStream_t st, int n_sm);
 
 // Largest count of the count V prune (smallest probabilities kept per thread).
-constexpr int kMaxVPruneCount = 8;
+constexpr int kMaxVPruneCount = 16;
 
 // Rows of queries per CTA of the attention kernel (granularity of partials).
 int attn_tile_rows(const AttnParams& p);
 cudaError_t launch_prog_attn(const AttnParams& p, cudaStream_t st, int n_sm);
-// tcgen05 kernel (QUANT and DENSE modes)
+// tcgen05 kernel (QUANT, DENSE and COMPAT modes, fp16 / bf16)
 int tc_tile_rows();
 cudaError_t launch_prog_attn_tc(const AttnParams& p, cudaStream_t st);
-// mma.sync kernel (COMPAT mode)
-cudaError_t launch_prog_attn_mma(const AttnParams& p, cudaStream_t st);
 // SIMT kernel for fp32 tensors (QUANT and DENSE modes, N <= f32_max_keys())
 int f32_tile_rows();
 int f32_max_keys();

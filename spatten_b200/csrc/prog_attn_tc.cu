@@ -26,6 +26,14 @@
 //   pass 2   S = Q'.K'; P = exp(S - m)/l; P' = P < v_thr ? 0 : P;
 //            O += P'V; column sums of P' -> token-importance partials.
 // DENSE runs pass 1 and pass 2 with S = q.k (fp16/bf16 operands).
+// COMPAT (the reference op's float planes, spatten_bert_ultimate.py:58-74 and
+// spatten_progressive_attention.py:38-60): one MMA of N = 128 per key tile
+// gives S = [q.k_msb | q.k_lsb] (the K stage holds the tile's k_msb rows and
+// then its k_lsb rows); for every criterion tile (32 or 64 rows x 32 or 64
+// keys) whose largest q.k_msb * sm_scale is below tile_thr the scores become
+// q.k_msb * sm_scale + q.k_lsb * sm_scale, else q.k_msb * sm_scale. The
+// softmax warps covering one criterion tile vote through shared memory and
+// an mbarrier (a warp vote for 32 x 32). Passes 1 and 2 as for DENSE.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -53,7 +61,7 @@ constexpr int kNP = 2;         // P buffers
 constexpr int kCsCols = 16;    // N of the column-sum MMA (16 identical columns)
 constexpr int kWarpTma = 8, kWarpMma = 9, kWarpExp = 10;
 
-enum Mode : int { kQuant = 0, kDense = 1 };
+enum Mode : int { kQuant = 0, kDense = 1, kCompat = 2 };
 
 // error codes: 0x100 | role << 4 | site
 enum : unsigned { kErrSoftmax = 0x110, kErrTma = 0x120, kErrMma = 0x130, kErrExp = 0x140 };
@@ -65,18 +73,21 @@ struct TcParams {
   CUtensorMap tm_v;   // V ([Z,Hkv,N,D])
 };
 
-template <int MODE, typename T, int D>
+template <int MODE, typename T, int D, bool VC>
 struct Layout {
   static constexpr int kAtoms = D / 64;                 // 128-byte K atoms of Q'/K' rows (2D bytes)
   static constexpr int kQBytes = kAtoms * BM * 128;     // Q' operand
-  static constexpr int kKBytes = kAtoms * BN * 128;     // K' operand stage
+  static constexpr int kKRows = (MODE == kCompat) ? 2 * BN : BN;  // K operand rows (COMPAT: msb | lsb)
+  static constexpr int kKBytes = kAtoms * kKRows * 128;  // K' operand stage
+  static constexpr int kSBuf = (MODE == kCompat) ? 1 : 2;  // S buffers in tensor memory
+  static constexpr int kSW = (MODE == kCompat) ? 2 * BN : BN;  // S columns per buffer
   static constexpr int kStgBytes = (MODE == kQuant) ? BN * D : 0;  // msb + lsb packed
   static constexpr int kVBytes = (D / 64) * BN * 128;   // V stage (MN-major blocks of 64 dims)
   static constexpr int kPBytes = BM * 128;              // P stage (64 keys x 2 B per row)
   static constexpr int kOnesBytes = 2 * kCsCols * 128;  // ones [16][128] (B of the column sums)
-  // tensor memory: S buffers [0, 2*BN), O [2*BN, 2*BN+D), column sums after O
-  static constexpr int kColO = 2 * BN;
-  static constexpr int kColCs = 2 * BN + D;
+  // tensor memory: S buffers [0, kSBuf*kSW), O (D columns), column sums after O
+  static constexpr int kColO = kSBuf * kSW;
+  static constexpr int kColCs = kColO + D;
   static constexpr uint32_t kTmemCols = (kColCs + 2 * kCsCols) <= 256 ? 256 : 512;
   static constexpr int oQ = 0;
   static constexpr int oK = oQ + kQBytes;
@@ -88,11 +99,16 @@ struct Layout {
   static constexpr int oKb = oKs + kNExp * BN * 4;      // float [kNExp][BN] key bias * log2e
   static constexpr int oSt = oKb + kNExp * BN * 4;      // float [2 (m,l)][2 halves][BM] row statistics
   static constexpr int oHs = oSt + 2 * 2 * BM * 4;      // float [kSoftWarps]
-  static constexpr int oBar = oHs + 4 * kSoftWarps;     // mbarriers
-  static constexpr int kNumBars = 2 * kNStg + 2 * kNExp + 2 * 2 + 2 * kNP + 2 * kNV + 2 * 2 + 3;
+  static constexpr int oVote = oHs + 4 * kSoftWarps;    // int [2][kSoftWarps] COMPAT tile votes
+  static constexpr int oBar = oVote + 2 * 4 * kSoftWarps;  // mbarriers
+  static constexpr int kNumBars = 2 * kNStg + 2 * kNExp + 2 * 2 + 2 * kNP + 2 * kNV + 2 * 2 + 3 + 8;
   static constexpr int oTmem = oBar + kNumBars * 8;
   static constexpr int oFlag = oTmem + 4;  // int abort, int decision, int key tiles of the CTA
-  static constexpr int kBytes = oFlag + 16;
+  // count V prune (VC): each softmax thread's kMaxVPruneCount smallest
+  // (score, key) pairs, float [kMaxVPruneCount][kSoftThreads] then int [..]
+  static constexpr int oCv = (oFlag + 16 + 15) & ~15;
+  static constexpr int kCvBytes = VC ? 2 * kMaxVPruneCount * kSoftThreads * 4 : 0;
+  static constexpr int kBytes = oCv + kCvBytes;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
@@ -112,6 +128,7 @@ struct Bars {
   uint64_t* q_ready;
   uint64_t* dec_ready;
   uint64_t* o_full;
+  uint64_t* vote;  // [2 buffers][4 vote groups] (COMPAT)
 };
 
 // Pairs of fp32 values for the packed (f32x2) FP instructions of sm_100.
@@ -142,7 +159,7 @@ constexpr float kMagic = 12582912.0f;
 
 template <int MODE, typename T, int D, bool VC>
 struct Cta {
-  using L = Layout<MODE, T, D>;
+  using L = Layout<MODE, T, D, VC>;
   const TcParams& P;
   const AttnParams& p;
   uint8_t* sm;  // 1024-aligned base
@@ -169,6 +186,7 @@ struct Cta {
     b.q_ready = bar++;
     b.dec_ready = bar++;
     b.o_full = bar++;
+    b.vote = bar; bar += 8;
     abort = reinterpret_cast<volatile int*>(sm + L::oFlag);
     decision = reinterpret_cast<int*>(sm + L::oFlag + 4);
     // With a causal mask or key limits the work grows with the row index:
@@ -231,6 +249,9 @@ struct Cta {
     mbar_init(b.q_ready, kSoftWarps);
     mbar_init(b.dec_ready, kSoftWarps);
     mbar_init(b.o_full, 1);
+    // COMPAT: one arrival per softmax warp of a criterion tile
+    const int vote_warps = (p.tile_m == 64 ? 2 : 1) * (p.tile_n == 64 ? 2 : 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&b.vote[i], vote_warps);
     *abort = 0;
     *decision = 0;
     fence_barrier_init();
@@ -246,7 +267,7 @@ struct Cta {
   SPATTEN_DEV void tma_role() {
     if ((threadIdx.x & 31) != 0) return;
     prefetch_tmap(&P.tm_k0);
-    if (MODE == kQuant) prefetch_tmap(&P.tm_k1);
+    if (MODE != kDense) prefetch_tmap(&P.tm_k1);
     prefetch_tmap(&P.tm_v);
     uint32_t t = 0, tv = 0;  // global tile counter, V tile counter
     int any = 0;
@@ -271,10 +292,13 @@ struct Cta {
           const int s = t % kNExp;
           if (!mbar_wait(&b.k_empty[s], ((t / kNExp) & 1) ^ 1, kErrTma | 3, abort)) { ok = false; break; }
           uint8_t* dst = sm + L::oK + s * L::kKBytes;
-          mbar_arrive_expect_tx(&b.k_full[s], BN * D * 2);
+          mbar_arrive_expect_tx(&b.k_full[s], L::kKRows * D * 2);
 #pragma unroll
-          for (int a = 0; a < D / 64; ++a)
-            tma_load_4d(dst + a * BN * 128, &P.tm_k0, 64 * a, n0, kvh, z, &b.k_full[s]);
+          for (int a = 0; a < D / 64; ++a) {
+            tma_load_4d(dst + a * L::kKRows * 128, &P.tm_k0, 64 * a, n0, kvh, z, &b.k_full[s]);
+            if (MODE == kCompat)  // the tile's k_lsb rows after its k_msb rows
+              tma_load_4d(dst + a * L::kKRows * 128 + BN * 128, &P.tm_k1, 64 * a, n0, kvh, z, &b.k_full[s]);
+          }
         }
         if (pass == 2) {
           const int s = tv % kNV;
@@ -410,7 +434,7 @@ struct Cta {
     if ((threadIdx.x & 31) != 0) return;
     constexpr uint32_t ab16 = std::is_same<T, __half>::value ? 0 : 1;
     constexpr uint32_t idesc_s = (MODE == kQuant) ? instr_desc(2, 1, 0, 0, BM, BN)
-                                                  : instr_desc(1, ab16, 0, 0, BM, BN);
+                                                  : instr_desc(1, ab16, 0, 0, BM, L::kSW);
     constexpr uint32_t idesc_pv = instr_desc(1, ab16, 0, 1, BM, D);
     constexpr uint32_t idesc_cs = instr_desc(1, ab16, 1, 0, BM, kCsCols);
     const bool want_tok = p.tok_partial != nullptr;
@@ -434,17 +458,17 @@ struct Cta {
       bool ok = true;
       for (int j = 0; j <= nt; ++j) {
         if (j < nt) {
-          const int es = t % kNExp, sb = t & 1;
+          const int es = t % kNExp, sb = t % L::kSBuf;
           if (!mbar_wait(&b.k_full[es], (t / kNExp) & 1, kErrMma | 3, abort)) { ok = false; break; }
-          if (!mbar_wait(&b.s_empty[sb], ((t >> 1) & 1) ^ 1, kErrMma | 4, abort)) { ok = false; break; }
+          if (!mbar_wait(&b.s_empty[sb], ((t / L::kSBuf) & 1) ^ 1, kErrMma | 4, abort)) { ok = false; break; }
           tc_fence_after();
           const uint32_t kaddr = smem_u32(sm + L::oK + es * L::kKBytes);
           for (int kk = 0; kk < nk; ++kk) {
             const int atom = kk >> 2, off = (kk & 3) * 32;
             const uint64_t ad = smem_desc_sw128(qaddr + atom * (BM * 128) + off, 16, 1024);
-            const uint64_t bd = smem_desc_sw128(kaddr + atom * (BN * 128) + off, 16, 1024);
-            if (MODE == kQuant) mma_i8(tmem + sb * BN, ad, bd, idesc_s, kk > 0);
-            else mma_f16(tmem + sb * BN, ad, bd, idesc_s, kk > 0);
+            const uint64_t bd = smem_desc_sw128(kaddr + atom * (L::kKRows * 128) + off, 16, 1024);
+            if (MODE == kQuant) mma_i8(tmem + sb * L::kSW, ad, bd, idesc_s, kk > 0);
+            else mma_f16(tmem + sb * L::kSW, ad, bd, idesc_s, kk > 0);
           }
           mma_commit(&b.s_full[sb]);
           mma_commit(&b.k_empty[es]);
@@ -578,19 +602,47 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
   uint32_t t = 0;
   bool alive = true;
 
+  // COMPAT: OR of `hot` over the softmax warps of one criterion tile (a warp
+  // covers 32 rows x 32 keys of the S tile; 64-row / 64-key criterion tiles
+  // span two or four warps, which vote through shared memory and an mbarrier
+  // per vote group, double-buffered over the tiles).
+  auto vote_group = [&](int w) {
+    const int wq = w & 3, wh = w >> 2;
+    return (p.tile_n == 64 ? 0 : wh) * (p.tile_m == 64 ? 2 : 4) + (p.tile_m == 64 ? wq / 2 : wq);
+  };
+  auto compat_vote = [&](bool hot, uint32_t tt) -> bool {
+    const bool wh = __any_sync(0xffffffffu, hot);
+    if (p.tile_m == 32 && p.tile_n == 32) return wh;
+    const int buf = tt & 1, grp = vote_group(warp);
+    int* votes = reinterpret_cast<int*>(sm + L::oVote) + buf * kSoftWarps;
+    if (lane == 0) votes[warp] = wh ? 1 : 0;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&b.vote[buf * 4 + grp]);
+    if (!mbar_wait(&b.vote[buf * 4 + grp], (tt >> 1) & 1, kErrSoftmax | 6, abort)) {
+      alive = false;
+      return true;
+    }
+    bool any = false;
+    for (int w = 0; w < kSoftWarps; ++w)
+      if (vote_group(w) == grp) any |= votes[w] != 0;
+    return any;
+  };
+
   // This thread's 32 scores of tile j (columns c0..c0+31 of the 64), as
   // log2-domain floats with key scale, bias and masks applied. With `dump`,
   // the integer scores also go to score_out.
   auto scores = [&](int j, float (&s)[HC], int32_t* dump) {
-    const int sb = t & 1, es = t % kNExp;
+    const int sb = t % L::kSBuf, es = t % kNExp;
     const uint32_t tt = t++;
     if (!alive) return;
-    if (!mbar_wait(&b.s_full[sb], (tt >> 1) & 1, kErrSoftmax | 1, abort)) { alive = false; return; }
+    if (!mbar_wait(&b.s_full[sb], (tt / L::kSBuf) & 1, kErrSoftmax | 1, abort)) { alive = false; return; }
     tc_fence_after();
     uint32_t* u = reinterpret_cast<uint32_t*>(s);
+    uint32_t lr[32];  // COMPAT: q.k_lsb of the same columns
     {
       uint32_t r0[32];
-      tmem_ld32(tl + sb * BN + c0, r0);
+      tmem_ld32(tl + sb * L::kSW + c0, r0);
+      if constexpr (MODE == kCompat) tmem_ld32(tl + sb * L::kSW + BN + c0, lr);
       tmem_wait_ld();
 #pragma unroll
       for (int i = 0; i < 32; ++i) u[i] = r0[i];
@@ -618,6 +670,23 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
         unpack_f2(a, s[i], s[i + 1]);
         unpack_f2(c, s[i + 2], s[i + 3]);
       }
+    } else if (MODE == kCompat) {
+      // the reference's rule: q.k_msb * sm_scale, plus q.k_lsb * sm_scale
+      // where the criterion tile's largest q.k_msb * sm_scale is below tile_thr
+      const float sc = p.sm_scale, thr = p.tile_thr;
+      const int lim_n = p.N - n0;
+      bool hot = false;
+#pragma unroll
+      for (int i = 0; i < HC; ++i) {
+        s[i] = __uint_as_float(u[i]) * sc;
+        hot |= (i < lim_n) && s[i] >= thr;
+      }
+      if (!compat_vote(valid && hot, tt)) {
+#pragma unroll
+        for (int i = 0; i < HC; ++i) s[i] = s[i] + __uint_as_float(lr[i]) * sc;
+      }
+#pragma unroll
+      for (int i = 0; i < HC; ++i) s[i] *= kLog2e;
     } else {
 #pragma unroll
       for (int i = 0; i < HC; ++i) s[i] = __uint_as_float(u[i]) * c2;
@@ -733,39 +802,43 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
                       : nullptr;
   f2 inv2 = pack_f2(0.f, 0.f), mn2 = pack_f2(0.f, 0.f);
   // Count V prune (VC): this thread's kMaxVPruneCount smallest (score, key)
-  // pairs of the scores its row ends up using, ascending in (score, key); the
-  // row's v_count-th smallest pair (kvs, kvn) then marks the keys to drop.
-  constexpr int KC = VC ? kMaxVPruneCount : 1;
-  float cv[KC];
-  int cn[KC];
+  // pairs of the scores its row ends up using, ascending in (score, key), in
+  // this thread's column of a shared-memory list (the largest entry cached in
+  // a register, so a score that does not enter the list costs one compare);
+  // the row's v_count-th smallest pair (kvs, kvn) then marks the keys to drop.
+  constexpr int KC = kMaxVPruneCount;
+  float* lv = reinterpret_cast<float*>(sm + L::oCv);
+  int* ln = reinterpret_cast<int*>(sm + L::oCv + KC * kSoftThreads * 4);
+  float cmax = INFINITY;
   float kvs = -INFINITY;
   int kvn = -1;
   auto track_reset = [&]() {
 #pragma unroll
     for (int q = 0; q < KC; ++q) {
-      cv[q] = INFINITY;
-      cn[q] = INT_MAX;
+      lv[q * kSoftThreads + tid] = INFINITY;
+      ln[q * kSoftThreads + tid] = INT_MAX;
     }
+    cmax = INFINITY;
   };
   auto track = [&](int j) {
     const int n0 = j * BN + c0;
     const int lim = p.N - n0;  // keys past N are not part of the row
 #pragma unroll
     for (int i = 0; i < HC; ++i) {
-      float x = s[i];
-      if (i < lim && x < cv[KC - 1]) {
-        int xn = n0 + i;
-#pragma unroll
-        for (int q = 0; q < KC; ++q) {
-          if (x < cv[q] || (x == cv[q] && xn < cn[q])) {
-            const float tv = cv[q];
-            const int tn = cn[q];
-            cv[q] = x;
-            cn[q] = xn;
-            x = tv;
-            xn = tn;
-          }
+      const float x = s[i];
+      // keys arrive in increasing order, so an equal score ranks after the
+      // entries already kept: only a smaller score enters the list
+      if (i < lim && x < cmax) {
+        int q = KC - 1;
+        for (; q > 0; --q) {
+          const float y = lv[(q - 1) * kSoftThreads + tid];
+          if (!(y > x)) break;
+          lv[q * kSoftThreads + tid] = y;
+          ln[q * kSoftThreads + tid] = ln[(q - 1) * kSoftThreads + tid];
         }
+        lv[q * kSoftThreads + tid] = x;
+        ln[q * kSoftThreads + tid] = n0 + i;
+        cmax = lv[(KC - 1) * kSoftThreads + tid];
       }
     }
   };
@@ -827,31 +900,22 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
       inv2 = pack_f2(inv_l, inv_l);
       mn2 = pack_f2(mneg, mneg);
       if (VC) {
-        // merge the two halves' lists (in P buffer 0, unused until the first
-        // P tile) up to the row's v_count-th smallest (score, key)
-        float* mvs = reinterpret_cast<float*>(sm + L::oP);
-        int* mns = reinterpret_cast<int*>(sm + L::oP + 2 * BM * KC * 4);
-#pragma unroll
-        for (int q = 0; q < KC; ++q) {
-          mvs[(hf * BM + r) * KC + q] = cv[q];
-          mns[(hf * BM + r) * KC + q] = cn[q];
-        }
+        // merge the row's two half-row lists up to the v_count-th smallest
+        // (score, key); both threads of the row find the same pair
         named_sync(1, kSoftThreads);
-        const float* va = mvs + r * KC;
-        const float* vb = mvs + (BM + r) * KC;
-        const int* na = mns + r * KC;
-        const int* nb = mns + (BM + r) * KC;
+        const int ta = tid & (kSoftThreads / 2 - 1), tb = ta + kSoftThreads / 2;
         int ia = 0, ib = 0;
         for (int q = 0; q < p.v_count; ++q) {
-          const float xa = ia < KC ? va[ia] : INFINITY, xb = ib < KC ? vb[ib] : INFINITY;
-          const int ya = ia < KC ? na[ia] : INT_MAX, yb = ib < KC ? nb[ib] : INT_MAX;
-          const bool ta = xa < xb || (xa == xb && ya < yb);
-          kvs = ta ? xa : xb;
-          kvn = ta ? ya : yb;
-          ia += ta ? 1 : 0;
-          ib += ta ? 0 : 1;
+          const float xa = ia < KC ? lv[ia * kSoftThreads + ta] : INFINITY;
+          const float xb = ib < KC ? lv[ib * kSoftThreads + tb] : INFINITY;
+          const int ya = ia < KC ? ln[ia * kSoftThreads + ta] : INT_MAX;
+          const int yb = ib < KC ? ln[ib * kSoftThreads + tb] : INT_MAX;
+          const bool pa = xa < xb || (xa == xb && ya < yb);
+          kvs = pa ? xa : xb;
+          kvn = pa ? ya : yb;
+          ia += pa ? 1 : 0;
+          ib += pa ? 0 : 1;
         }
-        named_sync(1, kSoftThreads);  // lists read before P overwrites the buffer
       }
     }
     for (int j = 0; j < nt; ++j) {
@@ -979,7 +1043,7 @@ template <int MODE, typename T, int D, bool VC>
 __global__ void __launch_bounds__(kThreads, (D == 64 && !VC) ? 2 : 1)
     prog_attn_tc_kernel(const __grid_constant__ TcParams P) {
   extern __shared__ uint8_t smem_raw[];
-  using L = Layout<MODE, T, D>;
+  using L = Layout<MODE, T, D, VC>;
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   Cta<MODE, T, D, VC> c(P, base);
@@ -1040,7 +1104,7 @@ cudaError_t make_map(CUtensorMap* m, CUtensorMapDataType dt, int esz, const void
 
 template <int MODE, typename T, int D, bool VC>
 cudaError_t launch_tc_t(const AttnParams& a, cudaStream_t st) {
-  using L = Layout<MODE, T, D>;
+  using L = Layout<MODE, T, D, VC>;
   TcParams P;
   memset(&P, 0, sizeof(P));
   P.a = a;
@@ -1059,6 +1123,11 @@ cudaError_t launch_tc_t(const AttnParams& a, cudaStream_t st) {
     e = make_map(&P.tm_k0, vdt, 2, a.k0, D, a.N, a.Hkv, a.Z, a.k_sn * 2, a.k_sh * 2, a.k_sz * 2, 64,
                  CU_TENSOR_MAP_SWIZZLE_128B);
     if (e != cudaSuccess) return e;
+    if (MODE == kCompat) {  // k_lsb: the same layout as k_msb
+      e = make_map(&P.tm_k1, vdt, 2, a.k1, D, a.N, a.Hkv, a.Z, a.k_sn * 2, a.k_sh * 2, a.k_sz * 2, 64,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+      if (e != cudaSuccess) return e;
+    }
   }
   e = make_map(&P.tm_v, vdt, 2, a.v, D, a.N, a.Hkv, a.Z, a.v_sn * 2, a.v_sh * 2, a.v_sz * 2, 64,
                CU_TENSOR_MAP_SWIZZLE_128B);
@@ -1086,7 +1155,23 @@ cudaError_t launch_prog_attn_tc(const AttnParams& a, cudaStream_t st) {
   const bool f16 = a.dtype == kF16;
   if (a.mode == kQuant) return f16 ? launch_tc_d<kQuant, __half>(a, st) : launch_tc_d<kQuant, __nv_bfloat16>(a, st);
   if (a.mode == kDense) return f16 ? launch_tc_d<kDense, __half>(a, st) : launch_tc_d<kDense, __nv_bfloat16>(a, st);
+  if (a.mode == kCompat) {
+    if (a.v_count > 0) return cudaErrorInvalidValue;
+    if (a.D == 64) return f16 ? launch_tc_t<kCompat, __half, 64, false>(a, st)
+                              : launch_tc_t<kCompat, __nv_bfloat16, 64, false>(a, st);
+    if (a.D == 128) return f16 ? launch_tc_t<kCompat, __half, 128, false>(a, st)
+                               : launch_tc_t<kCompat, __nv_bfloat16, 128, false>(a, st);
+  }
   return cudaErrorInvalidValue;
+}
+
+// fp16 / bf16 (every mode) on the tcgen05 kernel above, fp32 (QUANT, DENSE)
+// on the SIMT kernel.
+int attn_tile_rows(const AttnParams& p) { return p.dtype == kF32 ? f32_tile_rows() : tc_tile_rows(); }
+
+cudaError_t launch_prog_attn(const AttnParams& p, cudaStream_t st, int) {
+  if (p.dtype == kF32) return launch_prog_attn_f32(p, st);
+  return launch_prog_attn_tc(p, st);
 }
 
 cudaError_t read_device_error(unsigned int* code, bool reset) {

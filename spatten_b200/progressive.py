@@ -123,7 +123,7 @@ def prog_attn(q, k0, v, *, mode, k1=None, q_scale=None, k_scale=None, sm_scale=N
     """General progressive attention (see spatten_prog_attn_args in
     include/spatten_b200.h). ``q`` int8 for QUANT; ``k0``/``k1`` are the
     MSB/LSB planes (QUANT), k (DENSE) or k_msb/k_lsb (COMPAT).
-    ``v_prune_count`` (0..8) zeroes that many smallest probabilities of
+    ``v_prune_count`` (0..16) zeroes that many smallest probabilities of
     every row longer than it (the reference's count V prune). ``key_limit``
     [Z, M] int: row m of batch z sees keys n < key_limit[z, m] only (causal
     attention over a position-sorted subset of keys); replaces ``causal``.

@@ -24,7 +24,7 @@ attention core with the progressive sparse attention kernel:
   [B, Hkv, K_i, D] layout; ``kept_positions`` gives their positions.
 * Knobs: ``enable_token_prune`` with ``token_keep_ratio`` (or
   ``token_prune_num``), ``enable_v_prune`` with ``v_prune_threshold`` or the
-  count ``v_prune_num`` (<= 8), ``enable_prog_quant`` with ``quant_threshold``
+  count ``v_prune_num`` (<= 16), ``enable_prog_quant`` with ``quant_threshold``
   (the row max-probability below which the LSB plane of K is refetched).
 
 Prefill of unpadded batches only (the HF attention mask is not read: the

@@ -17,7 +17,8 @@ Fixtures:
   through the reference's ``spatten_encoder_forward`` +
   ``spatten_bert.SpattenBertSelfAttention``: pruning off, the reference's
   count knobs (the 0.9 ratios translated per layer),
-  the count V-prune, and a padded batch.
+  the count V-prune at v_prune_num = 2 (the module's default) and 16 (the
+  reference's benchmark setting, benchmark_seq_len.py), and a padded batch.
 * ``prog_compat.npz`` -- ``triton_progressive_qk`` (tile 32x32) at thresholds
   +100 / -100 / a mid value, and ``spatten_progressive_attention`` (tile
   64x64) at N=64 where it is exact.
@@ -104,7 +105,7 @@ def make_bert(ref_root):
     res = {"ids": ids.numpy(), "schedule": np.array(sched)}
     off, _, _ = ref_bert_run(ref_root, model, ids, mask, None)
     res["off_out"] = off
-    for tag, vp in (("casc", None), ("cascv", 2)):
+    for tag, vp in (("casc", None), ("cascv", 2), ("cascv16", 16)):
         out, heads, toks = ref_bert_run(ref_root, model, ids, mask, sched, vp)
         res[f"{tag}_out"] = out
         for i, (h, t) in enumerate(zip(heads, toks)):
@@ -181,7 +182,9 @@ def make_quant_extremes(ref_root):
 
 
 if __name__ == "__main__":
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
+    ref = sys.argv[1]
     make_compat(ref)
     make_quant_extremes(ref)
     make_bert(ref)

@@ -94,10 +94,10 @@ def test_prog_attn_requires_workspace():
     assert b"workspace" in N.lib.spatten_last_error()
 
 
-@pytest.mark.parametrize("count,mode,code", [(-1, 0, "ERR_INVALID"), (9, 0, "ERR_UNSUPPORTED"),
-                                             (9, 1, "ERR_UNSUPPORTED"), (2, 2, "ERR_UNSUPPORTED")])
+@pytest.mark.parametrize("count,mode,code", [(-1, 0, "ERR_INVALID"), (17, 0, "ERR_UNSUPPORTED"),
+                                             (17, 1, "ERR_UNSUPPORTED"), (2, 2, "ERR_UNSUPPORTED")])
 def test_count_v_prune_limits(count, mode, code):
-    """The count V prune takes 0..8 keys per row, QUANT and DENSE only."""
+    """The count V prune takes 0..16 keys per row, QUANT and DENSE only."""
     from spatten_b200 import _native as N
     a = _args(N, v_prune_count=count, mode=mode, tile_m=32, tile_n=32)
     assert N.lib.spatten_prog_attn(a, ctypes.c_void_p(0x1000), 1 << 20, None) == getattr(N, code)
@@ -239,3 +239,12 @@ def test_compact_out_proj_args_validation():
     assert N.lib.spatten_compact_out_proj(a, None) == N.ERR_INVALID
     a.res, a.L = 1 << 20, 0
     assert N.lib.spatten_compact_out_proj(a, None) == N.ERR_INVALID
+
+
+def test_compat_rejects_masks():
+    """The reference op has no mask: COMPAT refuses a bias, causal or key limit."""
+    from spatten_b200 import _native as N
+    for field, val in (("bias", 0x1000), ("causal", 1), ("key_limit", 0x1000)):
+        a = _args(N, mode=N.MODE_COMPAT, tile_m=32, tile_n=32)
+        setattr(a, field, val)
+        assert N.lib.spatten_prog_attn(a, None, 0, None) == N.ERR_UNSUPPORTED, field
