@@ -167,12 +167,15 @@ int spatten_prog_attn(const spatten_prog_attn_args* a, void* workspace, size_t w
  * counterpart in the reference, which has no C interface.
  *
  * The workspace comes from a fixed array of
- * spatten_prog_attn_noalloc_capacity() bytes (16 MiB) in device memory that
- * the library holds on every GPU that loads it, until the process exits; a
- * request needing more (spatten_prog_attn_workspace_size) fails with
- * SPATTEN_ERR_INVALID. Calls on one device share the array: calls that may
- * overlap on the GPU race, so order them on one stream. The first call on a
- * device looks up the array's address; make it before any stream capture.
+ * spatten_prog_attn_noalloc_capacity() bytes (16 MiB) in device memory,
+ * reserved on a GPU when the library's device code is loaded there (under
+ * CUDA's lazy module loading: at the first use of one of its kernels, which
+ * may be this call) and held until the process exits; a request needing more
+ * (spatten_prog_attn_workspace_size) fails with SPATTEN_ERR_INVALID. Calls on
+ * one device share the array: calls that may overlap on the GPU race, so
+ * order them on one stream. Each call looks up the array's address on the
+ * current device; the first call on a device may load the module there, so
+ * make it before any stream capture.
  */
 size_t spatten_prog_attn_noalloc_capacity(void);
 int spatten_prog_attn_noalloc(const spatten_prog_attn_args* a, void* stream);

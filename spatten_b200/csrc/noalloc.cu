@@ -14,17 +14,20 @@
 //  * The array holds kNoAllocBytes (16 MiB). A request whose workspace
 //    (spatten_prog_attn_workspace_size) exceeds that is rejected with
 //    SPATTEN_ERR_INVALID before anything runs.
-//  * Every GPU that loads the library holds the array until the process
-//    exits, whether or not this entry point is used.
+//  * The array is reserved on a device when the library's device code is
+//    loaded there -- at the first use of any of its kernels on that device
+//    under CUDA's default lazy module loading (which can be the first call of
+//    this entry point), at context creation with eager loading -- and it is
+//    held until the process exits.
 //  * All calls on a device share the one array and it keeps the last call's
 //    contents. The kernels write every partial sum they later read, so
 //    nothing has to start at zero. Calls that can overlap on the GPU (on
 //    different streams without ordering between them) race on the array;
 //    order them on one stream or with events.
-//  * The first call on a device looks up the array's device address
-//    (cudaGetSymbolAddress) with that device current; make that first call
-//    before any stream capture starts.
-#include <atomic>
+//  * Every call looks up the array's device address (cudaGetSymbolAddress)
+//    on the current device, so a call after cudaDeviceReset finds the array
+//    of the new context. The first call on a device may load the module
+//    there (lazy loading): make that first call before any stream capture.
 #include <cstdio>
 
 #include "../../include/spatten_b200.h"
@@ -38,23 +41,14 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
 namespace {
 
-constexpr int kMaxDevices = 64;
-std::atomic<void*> g_scratch_ptr[kMaxDevices];
-
-// Device address of the array on the current device (looked up once per device).
+// Device address of the array on the current device. Looked up on every call
+// rather than cached: a cached address would outlive the context it belongs
+// to after cudaDeviceReset.
 int scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return spatten::set_last_error(SPATTEN_ERR_CUDA, cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices)
-    return spatten::set_last_error(SPATTEN_ERR_UNSUPPORTED, "prog_attn_noalloc: device index out of range");
-  void* p = g_scratch_ptr[dev].load(std::memory_order_acquire);
-  if (!p) {
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p)
-      return spatten::set_last_error(SPATTEN_ERR_CUDA, "prog_attn_noalloc: cudaGetSymbolAddress failed");
-    g_scratch_ptr[dev].store(p, std::memory_order_release);
-  }
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || !p)
+    return spatten::set_last_error(SPATTEN_ERR_CUDA, "prog_attn_noalloc: cudaGetSymbolAddress failed");
   *out = p;
   return SPATTEN_OK;
 }

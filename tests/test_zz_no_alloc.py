@@ -8,8 +8,12 @@ call it through the C ABI twice in a row and compare each result with the
 allocating entry point (spatten_prog_attn) on the same inputs, and check that
 a request too large for the array is refused before anything runs.
 
-This file is collected last on purpose: it passes alone in a fresh process
-and after every other test.
+This file is named to be collected last so that, if it fails, a run that
+stops at the first failure (pytest -x) has already run every other test; no
+test depends on the order. It passes alone in a fresh process (where its
+first call is also the first use of the array on the device) and after every
+other test (where the array holds an earlier call's partial sums, which the
+second call of each test overwrites as well).
 """
 import ctypes
 
