@@ -59,7 +59,7 @@ UNIT = "tokens/s"
 TOKEN_KEEP = 0.9
 LAUNCHES_PER_STEP = 6  # quant Q, quant K planes, attention, token reduce, head reduce, top-k
 SWEEP_SEQS = (512, 2048, 4096, 8192)
-PEAKED_ALPHA = 1.0
+PEAKED_ALPHA = 2.0
 
 
 def parse():
@@ -80,6 +80,8 @@ def parse():
                     help="batch of the Qwen3 decode measurement (64; smaller for profiling captures)")
     ap.add_argument("--only-bert", action="store_true",
                     help="run only the BERT-base fp16 B32 S512 forward (one GPU) and print its line")
+    ap.add_argument("--micro", choices=MICRO_KERNELS,
+                    help="time one kernel's representative case (per-kernel profiling target)")
     ap.add_argument("--only-qwen3", action="store_true",
                     help="run only the Qwen3 prefill (--steps timed prefills) and print its line")
     return ap.parse_args()
@@ -545,28 +547,16 @@ def decode_bench(torch, rank, world, dev, steps=3, batch=DEC_B):
     qs = [torch.randn(batch, H, DEC_D, generator=g, device=dev, dtype=torch.bfloat16)
           for _ in range(DEC_LAYERS)]
     grp = dist.group.WORLD if world > 1 else None
-    st = torch.cuda.current_stream(dev)
 
     def step():
+        out = None
         for q in qs:
-            decode_attention(q, cache, top_k=DEC_TOPK, process_group=grp)
+            out = decode_attention(q, cache, top_k=DEC_TOPK, process_group=grp).out
+        return out
 
-    step()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(steps):
-        step()
-    e1.record(st)
-    torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1) / steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    # the 36-layer step (and, with several ranks, its 36 importance
+    # all-reduces) replayed as one CUDA graph: no host launch gaps
+    ms, kind, eager_ms, err = graph_timed(torch, dev, step, steps, world)
     # algorithmic bytes of one layer at one rank: the MSB plane and scale of
     # every cached key; both planes, the scale and V of every kept key; q, out
     per_layer = (batch * G * DEC_N * (DEC_D // 2 + 4) + batch * G * DEC_TOPK * (DEC_D + 2 * DEC_D + 4)
@@ -574,7 +564,8 @@ def decode_bench(torch, rank, world, dev, steps=3, batch=DEC_B):
     layer_ms = ms / DEC_LAYERS
     del cache, qs
     torch.cuda.empty_cache()
-    return {"ms_per_step": ms, "tokens_per_s": batch / (ms * 1e-3), "layer_ms": layer_ms,
+    return {"ms_per_step": ms, "launch": kind, "eager_ms_per_step": eager_ms, "graph_error": err,
+            "tokens_per_s": batch / (ms * 1e-3), "layer_ms": layer_ms,
             "hbm_gbs_per_gpu": per_layer / (layer_ms * 1e-3) / 1e9, "algorithmic_bytes_per_layer_gpu": per_layer,
             "batch": batch, "cache_len": DEC_N, "top_k": DEC_TOPK, "layers": DEC_LAYERS,
             "kv_heads_per_gpu": G, "dtype": "bf16",
@@ -878,6 +869,113 @@ def ours_arm(args, torch, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+MICRO_KERNELS = ("quant_q", "quant_k", "topk_decode", "topk_cascade", "gather", "op", "compat",
+                 "f32", "qk_norm_rope", "qkv_proj", "out_proj")
+
+
+def micro_bench(torch, dev, name, steps):
+    """One kernel's representative case, CUDA-event timed on the launching
+    stream (`steps` launches after 3 warm-ups), with its algorithmic bytes
+    (HBM-bound kernels) or flops: the target of the per-kernel ncu captures.
+    Inputs exceed the 126 MB L2 where the kernel is HBM-bound."""
+    import spatten_b200 as sp
+    from spatten_b200._native import MODE_COMPAT, MODE_DENSE, MODE_QUANT
+    g = torch.Generator(device=dev).manual_seed(7)
+    rn = lambda *shape, dt=torch.float16: torch.randn(*shape, generator=g, device=dev, dtype=dt)  # noqa: E731
+    info = {}
+    if name == "quant_q":
+        x = rn(16, 12, 8192, 64)
+        fn = lambda: sp.quant_q_int8(x)  # noqa: E731
+        rows = x.numel() // 64
+        info = dict(case="Q [16, 12, 8192, 64] fp16 -> int8 + scale", bytes=rows * (128 + 64 + 4))
+    elif name == "quant_k":
+        x = rn(16, 12, 8192, 64)
+        fn = lambda: sp.quant_k_planes(x)  # noqa: E731
+        rows = x.numel() // 64
+        info = dict(case="K [16, 12, 8192, 64] fp16 -> 4-bit planes + scale", bytes=rows * (128 + 64 + 4))
+    elif name == "topk_decode":
+        x = torch.rand(64, 32768, generator=g, device=dev)
+        fn = lambda: sp.topk_indices(x, 2048)  # noqa: E731
+        info = dict(case="top-2048 of [64, 32768] fp32 (decode)", bytes=x.numel() * 4 + 64 * 2048 * 8)
+    elif name == "topk_cascade":
+        x = torch.rand(32, 512, generator=g, device=dev)
+        fn = lambda: sp.topk_indices(x, 461)  # noqa: E731
+        info = dict(case="top-461 of [32, 512] fp32 (BERT cascade)", bytes=x.numel() * 4 + 32 * 461 * 8)
+    elif name == "gather":
+        h = rn(32, 4096, 768)
+        idx = torch.sort(torch.rand(32, 4096, generator=g, device=dev).topk(3687, dim=1).indices, 1).values
+        fn = lambda: sp.gather_rows(h, idx)  # noqa: E731
+        info = dict(case="kept rows [32, 3687 of 4096, 768] fp16", bytes=2 * 32 * 3687 * 768 * 2 + idx.numel() * 8)
+    elif name in ("op", "compat", "f32"):
+        if name == "f32":
+            q, k, v = (rn(8, 12, 1024, 64, dt=torch.float32) for _ in range(3))
+            q8, qs = sp.quant_q_int8(q)
+            kp = sp.quant_k_planes(k)
+            fn = lambda: sp.prog_attn(q8, kp.msb, v, k1=kp.lsb, mode=MODE_QUANT, q_scale=qs,  # noqa: E731
+                                      k_scale=kp.scale, sm_scale=SM_SCALE, refetch_thr=REFETCH_THR,
+                                      v_thr=V_THR, want_tok=True, want_head=True)
+            info = dict(case="fp32 progressive attention B8 H12 S1024 D64 (SIMT kernel)")
+        elif name == "compat":
+            q, k, v = (rn(B, H, S, D) for _ in range(3))
+            km, kl = (0.8 * k).half(), (0.2 * k).half()
+            fn = lambda: sp.prog_attn(q, km, v, k1=kl, mode=MODE_COMPAT, sm_scale=SM_SCALE,  # noqa: E731
+                                      tile=(32, 32), tile_thr=0.5)
+            info = dict(case=f"reference float-plane op, 32x32 tile rule, B{B} H{H} S{S} D{D} fp16",
+                        flops=2 * 2 * B * H * S * S * D + 2 * B * H * S * S * D)
+        else:
+            q, k, v = (t.to(dev) for t in make_inputs(SEED, S, torch))
+            q8, qs = sp.quant_q_int8(q)
+            kp = sp.quant_k_planes(k)
+            fn = lambda: sp.prog_attn(q8, kp.msb, v, k1=kp.lsb, mode=MODE_QUANT, q_scale=qs,  # noqa: E731
+                                      k_scale=kp.scale, sm_scale=SM_SCALE, refetch_thr=REFETCH_THR,
+                                      v_thr=V_THR, want_tok=True, want_head=True)
+            info = dict(case=f"progressive attention B{B} H{H} S{S} D{D} fp16 (the bench's launch)")
+    elif name == "qk_norm_rope":
+        from transformers import Qwen3Config
+        from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm, Qwen3RotaryEmbedding
+        from spatten_b200.qwen3 import qk_norm_rope
+        Bq, Sq = 4, 8192
+        cfg = Qwen3Config(hidden_size=1024, num_attention_heads=16, num_key_value_heads=8, head_dim=128,
+                          rope_theta=1e6, max_position_embeddings=Sq)
+        qn = Qwen3RMSNorm(128, eps=cfg.rms_norm_eps).to(dev, torch.bfloat16)
+        kn = Qwen3RMSNorm(128, eps=cfg.rms_norm_eps).to(dev, torch.bfloat16)
+        qp, kp_ = rn(Bq, Sq, 16 * 128, dt=torch.bfloat16), rn(Bq, Sq, 8 * 128, dt=torch.bfloat16)
+        cos, sin = Qwen3RotaryEmbedding(cfg, device=dev)(qp, torch.arange(Sq, device=dev)[None].expand(Bq, Sq))
+        fn = lambda: qk_norm_rope(qp, kp_, qn, kn, cos, sin, 16, 8, 128, True)  # noqa: E731
+        info = dict(case="Qwen3-0.6B QK-norm + RoPE + q int8, 4 x 8192 tokens, bf16",
+                    bytes=Bq * Sq * (24 * 128 * 2 + 2 * 128 * 2 * 2 + 8 * 128 * 2 + 16 * (128 + 4)))
+    elif name == "qkv_proj":
+        from spatten_b200.proj import qkv_proj
+        x = rn(32, 512, 768)
+        w = rn(3 * 768, 768) * 0.03
+        bias = rn(3 * 768)
+        fn = lambda: qkv_proj(x, w, bias, 12, 64, quantize=True)  # noqa: E731
+        info = dict(case="BERT layer-0 Q/K/V projection, 32 x 512 tokens x 768 -> 3 x 12 heads, "
+                         "Q / K quantised in the epilogue", flops=2 * 32 * 512 * 768 * 3 * 768)
+    elif name == "out_proj":
+        from spatten_b200.proj import compact_out_proj
+        ctx = rn(32, 512, 768)
+        res = rn(32, 512, 768)
+        kept = torch.sort(torch.rand(32, 512, generator=g, device=dev).topk(461, dim=1).indices, 1).values
+        w = rn(768, 768) * 0.03
+        bias = rn(768)
+        heads = torch.arange(12, device=dev)
+        fn = lambda: compact_out_proj(ctx, res, kept, w, bias, 12, 64, heads=heads)  # noqa: E731
+        info = dict(case="BERT output projection on the kept rows, 32 x 461 of 512 rows, 768 -> 768, "
+                         "bias + gathered residual", flops=2 * 32 * 461 * 768 * 768)
+    else:
+        raise ValueError(f"--micro {name}: one of {', '.join(MICRO_KERNELS)}")
+    for _ in range(3):
+        fn()
+    us = time_steps(torch, dev, fn, steps) * 1e3
+    out = dict(metric="micro_us_per_launch", kernel=name, value=us, unit="us", steps=steps, **info)
+    if "bytes" in info:
+        out["achieved_gbs"] = info["bytes"] / (us * 1e-6) / 1e9
+    if "flops" in info:
+        out["achieved_tflops"] = info["flops"] / (us * 1e-6) / 1e12
+    return out
+
+
 def main():
     args = parse()
     import torch
@@ -913,6 +1011,11 @@ def main():
             r = bert_bench(torch, 0, 1, dev, steps=args.steps)
             print(json.dumps(dict(metric="bert_ms_per_batch", value=r["ms_per_batch"], unit="ms",
                                   higher_is_better=False, n_gpus=1, **r)), flush=True)
+        return
+    if args.micro:
+        dev = torch.device("cuda", local_rank)
+        torch.cuda.set_device(dev)
+        print(json.dumps(micro_bench(torch, dev, args.micro, args.steps)), flush=True)
         return
     if args.only_qwen3:
         if rank == 0:

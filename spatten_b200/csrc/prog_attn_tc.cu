@@ -51,15 +51,20 @@ using namespace sm100;
 
 constexpr int BM = 128;        // query rows per CTA (= TMEM lanes)
 constexpr int BN = 64;         // keys per tile
-constexpr int kSoftWarps = 8;  // two per TMEM lane quarter, 32 columns each
+constexpr int kSoftWarps = 4;  // one thread per query row, all 64 columns of a tile
 constexpr int kSoftThreads = kSoftWarps * 32;
-constexpr int kThreads = 384;  // 12 warps
+// Expander warps (64 / 32 keys of a 64-key tile per thread).
+#ifndef SPATTEN_TC_EXP_WARPS
+#define SPATTEN_TC_EXP_WARPS 2
+#endif
+constexpr int kExpWarps = SPATTEN_TC_EXP_WARPS;
+constexpr int kThreads = (kSoftWarps + 2 + kExpWarps) * 32;
 constexpr int kNStg = 3;       // packed-plane staging stages (QUANT)
 constexpr int kNExp = 2;       // K operand stages
 constexpr int kNV = 2;         // V stages
 constexpr int kNP = 2;         // P buffers
 constexpr int kCsCols = 16;    // N of the column-sum MMA (16 identical columns)
-constexpr int kWarpTma = 8, kWarpMma = 9, kWarpExp = 10;
+constexpr int kWarpTma = kSoftWarps, kWarpMma = kSoftWarps + 1, kWarpExp = kSoftWarps + 2;
 
 enum Mode : int { kQuant = 0, kDense = 1, kCompat = 2 };
 
@@ -97,8 +102,7 @@ struct Layout {
   static constexpr int oOnes = oStg + kNStg * kStgBytes;  // 1024-aligned
   static constexpr int oKs = oOnes + kOnesBytes;        // float [kNExp][BN] key scale
   static constexpr int oKb = oKs + kNExp * BN * 4;      // float [kNExp][BN] key bias * log2e
-  static constexpr int oSt = oKb + kNExp * BN * 4;      // float [2 (m,l)][2 halves][BM] row statistics
-  static constexpr int oHs = oSt + 2 * 2 * BM * 4;      // float [kSoftWarps]
+  static constexpr int oHs = oKb + kNExp * BN * 4;      // float [kSoftWarps]
   static constexpr int oVote = oHs + 4 * kSoftWarps;    // int [2][kSoftWarps] COMPAT tile votes
   static constexpr int oBar = oVote + 2 * 4 * kSoftWarps;  // mbarriers
   static constexpr int kNumBars = 2 * kNStg + 2 * kNExp + 2 * 2 + 2 * kNP + 2 * kNV + 2 * 2 + 3 + 8;
@@ -226,10 +230,10 @@ struct Cta {
   SPATTEN_DEV void init_barriers() {
     for (int i = 0; i < kNStg; ++i) {
       mbar_init(&b.stg_full[i], 1);
-      mbar_init(&b.stg_empty[i], 2);
+      mbar_init(&b.stg_empty[i], kExpWarps);
     }
     for (int i = 0; i < kNExp; ++i) {
-      mbar_init(&b.k_full[i], MODE == kQuant ? 2 : 3);
+      mbar_init(&b.k_full[i], MODE == kQuant ? kExpWarps : 1 + kExpWarps);
       mbar_init(&b.k_empty[i], 1 + kSoftWarps);
     }
     for (int i = 0; i < 2; ++i) {
@@ -249,9 +253,8 @@ struct Cta {
     mbar_init(b.q_ready, kSoftWarps);
     mbar_init(b.dec_ready, kSoftWarps);
     mbar_init(b.o_full, 1);
-    // COMPAT: one arrival per softmax warp of a criterion tile
-    const int vote_warps = (p.tile_m == 64 ? 2 : 1) * (p.tile_n == 64 ? 2 : 1);
-    for (int i = 0; i < 8; ++i) mbar_init(&b.vote[i], vote_warps);
+    // COMPAT: one arrival per softmax warp of a 64-row criterion tile
+    for (int i = 0; i < 8; ++i) mbar_init(&b.vote[i], 2);
     *abort = 0;
     *decision = 0;
     fence_barrier_init();
@@ -334,7 +337,8 @@ struct Cta {
 
   // ------------------------------------------------------------- expander
   SPATTEN_DEV void expand_role() {
-    const int e = threadIdx.x - kWarpExp * 32;  // key within the tile, 0..63
+    constexpr int KPT = BN / (kExpWarps * 32);  // keys of a tile per expander thread
+    const int e0 = threadIdx.x - kWarpExp * 32;  // this thread's first key within the tile
     const int lane = threadIdx.x & 31;
     const float* ksrc = (MODE == kQuant) ? p.k_scale + ((int64_t)z * p.Hkv + kvh) * p.N : nullptr;
     const bool key_bias = p.bias != nullptr && p.b_sm == 0;
@@ -349,82 +353,92 @@ struct Cta {
       }
       const bool lsb = pass_uses_lsb(pass, any);
       // key scale / bias of tile j, loaded one tile ahead to hide the latency
-      auto fetch = [&](int j, float& ks, float& kb) {
-        const int n = j * BN + e;
-        ks = 0.f;
-        kb = 0.f;
-        if (j < nt && n < p.N) {
-          if (MODE == kQuant) ks = __ldg(ksrc + n);
-          if (key_bias) kb = __ldg(bsrc + (int64_t)n * p.b_sn) * kLog2e;
+      auto fetch = [&](int j, float (&ks)[KPT], float (&kb)[KPT]) {
+#pragma unroll
+        for (int k = 0; k < KPT; ++k) {
+          const int n = j * BN + e0 + k * kExpWarps * 32;
+          ks[k] = 0.f;
+          kb[k] = 0.f;
+          if (j < nt && n < p.N) {
+            if (MODE == kQuant) ks[k] = __ldg(ksrc + n);
+            if (key_bias) kb[k] = __ldg(bsrc + (int64_t)n * p.b_sn) * kLog2e;
+          }
         }
       };
-      float ks_next, kb_next;
+      float ks_next[KPT], kb_next[KPT];
       fetch(0, ks_next, kb_next);
       for (int j = 0; j < nt; ++j, ++t) {
-        const float ks = ks_next, kb = kb_next;
-        fetch(j + 1, ks_next, kb_next);
-        const int es = t % kNExp;
-        uint32_t X[D / 8], Y[D / 8];
-        if (MODE == kQuant) {
-          const int s = t % kNStg;
-          if (!mbar_wait(&b.stg_full[s], (t / kNStg) & 1, kErrExp | 2, abort)) return;
-          // staging rows of D/2 bytes land with the TMA's 32-byte (D=64) or
-          // 64-byte (D=128) swizzle: 16-byte chunk c of row e sits at c ^ sw
-          const int sw = (D == 64) ? ((e >> 2) & 1) : ((e >> 1) & 3);
-          const uint4* src = reinterpret_cast<const uint4*>(sm + L::oStg + s * L::kStgBytes + e * (D / 2));
+        float ks[KPT], kb[KPT];
 #pragma unroll
-          for (int i = 0; i < D / 32; ++i) {
-            const uint4 v = src[i ^ sw];
-            X[4 * i] = v.x; X[4 * i + 1] = v.y; X[4 * i + 2] = v.z; X[4 * i + 3] = v.w;
-          }
-          if (lsb) {
-            const uint4* srcl = reinterpret_cast<const uint4*>(sm + L::oStg + s * L::kStgBytes +
-                                                               BN * (D / 2) + e * (D / 2));
+        for (int k = 0; k < KPT; ++k) {
+          ks[k] = ks_next[k];
+          kb[k] = kb_next[k];
+        }
+        fetch(j + 1, ks_next, kb_next);
+        const int es = t % kNExp, s = t % kNStg;
+        if (MODE == kQuant && !mbar_wait(&b.stg_full[s], (t / kNStg) & 1, kErrExp | 2, abort)) return;
+        if (!mbar_wait(&b.k_empty[es], ((t / kNExp) & 1) ^ 1, kErrExp | 3, abort)) return;
+#pragma unroll
+        for (int k = 0; k < KPT; ++k) {
+          const int e = e0 + k * kExpWarps * 32;
+          if (MODE == kQuant) {
+            uint32_t X[D / 8], Y[D / 8];
+            // staging rows of D/2 bytes land with the TMA's 32-byte (D=64) or
+            // 64-byte (D=128) swizzle: 16-byte chunk c of row e sits at c ^ sw
+            const int sws = (D == 64) ? ((e >> 2) & 1) : ((e >> 1) & 3);
+            const uint4* src = reinterpret_cast<const uint4*>(sm + L::oStg + s * L::kStgBytes + e * (D / 2));
 #pragma unroll
             for (int i = 0; i < D / 32; ++i) {
-              const uint4 v = srcl[i ^ sw];
-              Y[4 * i] = v.x; Y[4 * i + 1] = v.y; Y[4 * i + 2] = v.z; Y[4 * i + 3] = v.w;
+              const uint4 v = src[i ^ sws];
+              X[4 * i] = v.x; X[4 * i + 1] = v.y; X[4 * i + 2] = v.z; X[4 * i + 3] = v.w;
             }
-          }
-          // The stage is read through the generic proxy and refilled by the
-          // TMA (async proxy) as soon as it is released: without a proxy fence
-          // between the reads and the release, the next tile's bytes could land
-          // before these reads were performed (seen with two CTAs per SM).
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&b.stg_empty[s]);
-        }
-        if (!mbar_wait(&b.k_empty[es], ((t / kNExp) & 1) ^ 1, kErrExp | 3, abort)) return;
-        if (MODE == kQuant) {
-          // K' row = [16*msb (D bytes) | lsb (D bytes)], K-major, 128B swizzle
-          uint8_t* row = sm + L::oK + es * L::kKBytes;
-          const int sw = e & 7;
-          auto put = [&](int byte_off, uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
-            const int atom = byte_off >> 7, chunk = (byte_off >> 4) & 7;
-            *reinterpret_cast<uint4*>(row + atom * (BN * 128) + e * 128 + ((chunk ^ sw) << 4)) =
-                make_uint4(w0, w1, w2, w3);
-          };
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {  // 16 packed bytes -> 16 dims lo + 16 dims hi
-            const uint32_t* x = X + 4 * c;
-            put(16 * c, (x[0] << 4) & 0xF0F0F0F0u, (x[1] << 4) & 0xF0F0F0F0u,
-                (x[2] << 4) & 0xF0F0F0F0u, (x[3] << 4) & 0xF0F0F0F0u);
-            put(D / 2 + 16 * c, x[0] & 0xF0F0F0F0u, x[1] & 0xF0F0F0F0u, x[2] & 0xF0F0F0F0u,
-                x[3] & 0xF0F0F0F0u);
             if (lsb) {
-              const uint32_t* y = Y + 4 * c;
-              put(D + 16 * c, y[0] & 0x0F0F0F0Fu, y[1] & 0x0F0F0F0Fu, y[2] & 0x0F0F0F0Fu,
-                  y[3] & 0x0F0F0F0Fu);
-              put(D + D / 2 + 16 * c, (y[0] >> 4) & 0x0F0F0F0Fu, (y[1] >> 4) & 0x0F0F0F0Fu,
-                  (y[2] >> 4) & 0x0F0F0F0Fu, (y[3] >> 4) & 0x0F0F0F0Fu);
+              const uint4* srcl = reinterpret_cast<const uint4*>(sm + L::oStg + s * L::kStgBytes +
+                                                                 BN * (D / 2) + e * (D / 2));
+#pragma unroll
+              for (int i = 0; i < D / 32; ++i) {
+                const uint4 v = srcl[i ^ sws];
+                Y[4 * i] = v.x; Y[4 * i + 1] = v.y; Y[4 * i + 2] = v.z; Y[4 * i + 3] = v.w;
+              }
             }
+            // K' row = [16*msb (D bytes) | lsb (D bytes)], K-major, 128B swizzle
+            uint8_t* row = sm + L::oK + es * L::kKBytes;
+            const int sw = e & 7;
+            auto put = [&](int byte_off, uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+              const int atom = byte_off >> 7, chunk = (byte_off >> 4) & 7;
+              *reinterpret_cast<uint4*>(row + atom * (BN * 128) + e * 128 + ((chunk ^ sw) << 4)) =
+                  make_uint4(w0, w1, w2, w3);
+            };
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {  // 16 packed bytes -> 16 dims lo + 16 dims hi
+              const uint32_t* x = X + 4 * c;
+              put(16 * c, (x[0] << 4) & 0xF0F0F0F0u, (x[1] << 4) & 0xF0F0F0F0u,
+                  (x[2] << 4) & 0xF0F0F0F0u, (x[3] << 4) & 0xF0F0F0F0u);
+              put(D / 2 + 16 * c, x[0] & 0xF0F0F0F0u, x[1] & 0xF0F0F0F0u, x[2] & 0xF0F0F0F0u,
+                  x[3] & 0xF0F0F0F0u);
+              if (lsb) {
+                const uint32_t* y = Y + 4 * c;
+                put(D + 16 * c, y[0] & 0x0F0F0F0Fu, y[1] & 0x0F0F0F0Fu, y[2] & 0x0F0F0F0Fu,
+                    y[3] & 0x0F0F0F0Fu);
+                put(D + D / 2 + 16 * c, (y[0] >> 4) & 0x0F0F0F0Fu, (y[1] >> 4) & 0x0F0F0F0Fu,
+                    (y[2] >> 4) & 0x0F0F0F0Fu, (y[3] >> 4) & 0x0F0F0F0Fu);
+              }
+            }
+            reinterpret_cast<float*>(sm + L::oKs)[es * BN + e] = ks[k];
           }
-          reinterpret_cast<float*>(sm + L::oKs)[es * BN + e] = ks;
+          reinterpret_cast<float*>(sm + L::oKb)[es * BN + e] = kb[k];
         }
-        reinterpret_cast<float*>(sm + L::oKb)[es * BN + e] = kb;
+        // One proxy fence covers both hand-offs: the staging stage, read
+        // through the generic proxy, is refilled by the TMA (async proxy) as
+        // soon as it is released -- without the fence the next tile's bytes
+        // could land before these reads were performed (seen with two CTAs
+        // per SM) -- and the K' rows written here are read by the MMA.
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&b.k_full[es]);
+        if (lane == 0) {
+          if (MODE == kQuant) mbar_arrive(&b.stg_empty[s]);
+          mbar_arrive(&b.k_full[es]);
+        }
       }
     }
   }
@@ -529,13 +543,13 @@ struct Cta {
 
   // -------------------------------------------------------------- softmax
   SPATTEN_DEV void softmax_role();
-  SPATTEN_DEV void load_q_row(int r, bool valid, int hf);
+  SPATTEN_DEV void load_q_row(int r, bool valid);
 };
 
-// Q row r -> Q' operand (first D bytes for QUANT, 2D bytes for DENSE), zeros
-// if invalid; the two softmax threads of a row load alternate halves.
+// Q row r -> Q' operand (first D bytes for QUANT, 2D bytes for DENSE and
+// COMPAT), zeros if invalid.
 template <int MODE, typename T, int D, bool VC>
-SPATTEN_DEV void Cta<MODE, T, D, VC>::load_q_row(int r, bool valid, int hf) {
+SPATTEN_DEV void Cta<MODE, T, D, VC>::load_q_row(int r, bool valid) {
   const int row = m0 + r;
   uint8_t* base = sm + L::oQ;
   const int sw = r & 7;
@@ -544,7 +558,8 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::load_q_row(int r, bool valid, int hf) {
   const uint8_t* src = static_cast<const uint8_t*>(p.q) +
                        ((int64_t)z * p.q_sz + (int64_t)h * p.q_sh + (int64_t)row * p.q_sm) * esz;
   const bool al16 = ((reinterpret_cast<uintptr_t>(src)) & 15) == 0;
-  for (int c = hf * (kChunks / 2); c < (hf + 1) * (kChunks / 2); ++c) {
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
     uint4 v = make_uint4(0, 0, 0, 0);
     if (valid) {
       if (al16) {
@@ -560,35 +575,82 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::load_q_row(int r, bool valid, int hf) {
   }
 }
 
+// max(a, b, c) in one instruction
+SPATTEN_DEV float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// 2^x for x <= 0 on the FMA pipe instead of the MUFU (Cody-Waite range
+// reduction: x = n + f with n = rint(x), f in [-1/2, 1/2]; 2^f by the Taylor
+// series of exp(f ln 2) to degree 6: relative error below 2.5e-7 in fp32
+// (1.6e-7 from the series); 2^n added to the exponent field). Inputs below -127 (and -inf)
+// give 0 or a subnormal below 6e-39. Part of a tile's exponentials go here
+// so that the MUFU and the FMA pipe share them.
+SPATTEN_DEV float exp2_fma(float x) {
+  constexpr float kRnd = 12582912.0f;  // 1.5 * 2^23: x + kRnd rounds x to an integer
+  const float xc = fmaxf(x, -127.0f);
+  const float j = xc + kRnd;
+  const float f = xc - (j - kRnd);
+  // (ln 2)^k / k!, k = 6 .. 1
+  float p = 1.5403530393381608e-4f;
+  p = fmaf(p, f, 1.3333558146428443e-3f);
+  p = fmaf(p, f, 9.6181291076284772e-3f);
+  p = fmaf(p, f, 5.5504108664821580e-2f);
+  p = fmaf(p, f, 2.4022650695910071e-1f);
+  p = fmaf(p, f, 6.9314718055994531e-1f);
+  p = fmaf(p, f, 1.0f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+}
+#ifndef SPATTEN_TC_FMA_EXP
+#define SPATTEN_TC_FMA_EXP 0
+#endif
+// which of the four exponential chains of a tile run on the FMA pipe
+SPATTEN_DEV float exp2_split(float x, int chain) {
+  return (SPATTEN_TC_FMA_EXP && chain == 3) ? exp2_fma(x) : fast_exp2(x);
+}
+
+// 1.0f if a >= b, else 0.0f
+SPATTEN_DEV float ge_one(float a, float b) {
+  float d;
+  asm("set.ge.f32.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+// One softmax thread per query row (TMEM lane = row) owns all 64 columns of
+// a key tile: the row statistics are thread-local. A score is carried as a
+// value s whose log2-domain score is s * cse: without a bias s is the
+// unscaled product (QUANT: the exact integer score times the key scale;
+// DENSE: q.k; COMPAT: the reference's tile-rule score) and cse the row scale
+// (q scale * sm_scale * log2 e), which the exponent's FMA applies; with a
+// bias (or a zero row scale) s is the scaled, biased score and cse = 1.
 template <int MODE, typename T, int D, bool VC>
 SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
-  constexpr int HC = BN / 2;        // columns per softmax thread and tile
   const int tid = threadIdx.x;      // 0 .. kSoftThreads-1
   const int warp = tid >> 5, lane = tid & 31;
-  const int qd = warp & 3;          // TMEM lane quarter
-  const int hf = warp >> 2;         // which 32 of the tile's 64 columns
-  const int r = qd * 32 + lane;     // row within the tile = TMEM lane
-  const int c0 = hf * HC;
+  const int r = tid;                // row within the tile = TMEM lane
   const int row = m0 + r;
   const bool valid = row < p.M;
-  const uint32_t tl = tmem + ((uint32_t)(qd * 32) << 16);
-  float c2 = 0.f;
+  const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+  float cs = 0.f;
   if (valid) {
-    c2 = (MODE == kQuant) ? p.q_scale[((int64_t)z * p.H + h) * p.M + row] * p.sm_scale * kLog2e
-                          : p.sm_scale * kLog2e;
+    cs = (MODE == kQuant) ? p.q_scale[((int64_t)z * p.H + h) * p.M + row] * p.sm_scale * kLog2e
+         : (MODE == kCompat) ? kLog2e : p.sm_scale * kLog2e;
   }
+  const bool key_bias = p.bias != nullptr && p.b_sm == 0;
+  const bool gen_bias = p.bias != nullptr && p.b_sm != 0;
+  const bool prescale = key_bias || gen_bias || !(cs > 0.f);
+  const float cse = prescale ? 1.f : cs;
   {  // ones block: B operand of the column-sum MMA (every element 1.0)
     const uint32_t one2 = pack2<T>(1.f, 1.f);
     uint4* ob = reinterpret_cast<uint4*>(sm + L::oOnes);
     for (int i = tid; i < L::kOnesBytes / 16; i += kSoftThreads) ob[i] = make_uint4(one2, one2, one2, one2);
   }
-  load_q_row(r, valid, hf);
+  load_q_row(r, valid);
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) mbar_arrive(b.q_ready);
 
-  const bool key_bias = p.bias != nullptr && p.b_sm == 0;
-  const bool gen_bias = p.bias != nullptr && p.b_sm != 0;
   const float* brow = gen_bias ? p.bias + (int64_t)z * p.b_sz + (int64_t)h * p.b_sh + (int64_t)row * p.b_sm
                                : nullptr;
   const int shift = p.N - p.M;
@@ -597,185 +659,166 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
                                : (p.causal ? row + shift + 1 : p.N);
   const float* ksm = reinterpret_cast<const float*>(sm + L::oKs);
   const float* kbm = reinterpret_cast<const float*>(sm + L::oKb);
-  float* stm = reinterpret_cast<float*>(sm + L::oSt);  // [2][2][BM]
 
   uint32_t t = 0;
   bool alive = true;
 
-  // COMPAT: OR of `hot` over the softmax warps of one criterion tile (a warp
-  // covers 32 rows x 32 keys of the S tile; 64-row / 64-key criterion tiles
-  // span two or four warps, which vote through shared memory and an mbarrier
-  // per vote group, double-buffered over the tiles).
-  auto vote_group = [&](int w) {
-    const int wq = w & 3, wh = w >> 2;
-    return (p.tile_n == 64 ? 0 : wh) * (p.tile_m == 64 ? 2 : 4) + (p.tile_m == 64 ? wq / 2 : wq);
-  };
-  auto compat_vote = [&](bool hot, uint32_t tt) -> bool {
-    const bool wh = __any_sync(0xffffffffu, hot);
-    if (p.tile_m == 32 && p.tile_n == 32) return wh;
-    const int buf = tt & 1, grp = vote_group(warp);
-    int* votes = reinterpret_cast<int*>(sm + L::oVote) + buf * kSoftWarps;
-    if (lane == 0) votes[warp] = wh ? 1 : 0;
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&b.vote[buf * 4 + grp]);
-    if (!mbar_wait(&b.vote[buf * 4 + grp], (tt >> 1) & 1, kErrSoftmax | 6, abort)) {
-      alive = false;
-      return true;
+  // COMPAT: OR over the criterion tile of "some q.k_msb * sm_scale >= thr",
+  // separately for the tile's two 32-key halves. A warp covers 32 rows; a
+  // 64-row criterion tile spans two warps, which vote through shared memory
+  // and an mbarrier (double-buffered over the key tiles).
+  auto compat_vote = [&](bool hlo, bool hhi, uint32_t tt, bool& any_lo, bool& any_hi) {
+    bool wlo = __any_sync(0xffffffffu, hlo), whi = __any_sync(0xffffffffu, hhi);
+    if (p.tile_n == 64) wlo = whi = (wlo || whi);
+    if (p.tile_m == 64) {
+      const int buf = tt & 1, grp = warp >> 1;
+      int* votes = reinterpret_cast<int*>(sm + L::oVote) + buf * kSoftWarps;
+      if (lane == 0) votes[warp] = (wlo ? 1 : 0) | (whi ? 2 : 0);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b.vote[buf * 4 + grp]);
+      if (!mbar_wait(&b.vote[buf * 4 + grp], (tt >> 1) & 1, kErrSoftmax | 6, abort)) {
+        alive = false;
+        wlo = whi = true;
+      } else {
+        const int v = votes[2 * grp] | votes[2 * grp + 1];
+        wlo = (v & 1) != 0;
+        whi = (v & 2) != 0;
+      }
     }
-    bool any = false;
-    for (int w = 0; w < kSoftWarps; ++w)
-      if (vote_group(w) == grp) any |= votes[w] != 0;
-    return any;
+    any_lo = wlo;
+    any_hi = whi;
   };
 
-  // This thread's 32 scores of tile j (columns c0..c0+31 of the 64), as
-  // log2-domain floats with key scale, bias and masks applied. With `dump`,
-  // the integer scores also go to score_out.
-  auto scores = [&](int j, float (&s)[HC], int32_t* dump) {
+  // This row's 64 scores of key tile j (see the function comment for their
+  // scaling); keys past N and keys the row does not see are -inf. With
+  // `dump`, the integer scores also go to score_out.
+  auto scores = [&](int j, float (&s)[BN], int32_t* dump) {
     const int sb = t % L::kSBuf, es = t % kNExp;
     const uint32_t tt = t++;
     if (!alive) return;
     if (!mbar_wait(&b.s_full[sb], (tt / L::kSBuf) & 1, kErrSoftmax | 1, abort)) { alive = false; return; }
     tc_fence_after();
-    uint32_t* u = reinterpret_cast<uint32_t*>(s);
-    uint32_t lr[32];  // COMPAT: q.k_lsb of the same columns
-    {
-      uint32_t r0[32];
-      tmem_ld32(tl + sb * L::kSW + c0, r0);
-      if constexpr (MODE == kCompat) tmem_ld32(tl + sb * L::kSW + BN + c0, lr);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) u[i] = r0[i];
+    tmem_ld32f(tl + sb * L::kSW, s);
+    tmem_ld32f(tl + sb * L::kSW + 32, s + 32);
+    tmem_wait_ld();
+    const int n0 = j * BN;
+    if (MODE != kCompat) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b.s_empty[sb]);
     }
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&b.s_empty[sb]);
-    const int n0 = j * BN + c0;
-    if (dump && valid && row % p.score_rs == 0) {
-      for (int i = 0; i < HC; ++i)
-        if (n0 + i < p.N) dump[(int64_t)(row / p.score_rs) * p.N + n0 + i] = (int32_t)u[i];
+    if (MODE == kQuant && dump && valid && row % p.score_rs == 0) {
+      int32_t* d = dump + (int64_t)(row / p.score_rs) * p.N + n0;
+      for (int i = 0; i < BN; ++i)
+        if (n0 + i < p.N) d[i] = (int32_t)__float_as_uint(s[i]);
     }
     if (!mbar_wait(&b.k_full[es], (tt / kNExp) & 1, kErrSoftmax | 2, abort)) { alive = false; return; }
-    const float* ks = ksm + es * BN + c0;
-    const float* kb = kbm + es * BN + c0;
     if (MODE == kQuant) {
-      const f2 c22 = pack_f2(c2, c2);
+      // exact int32 -> fp32 (|x| < 2^22): the bits of 1.5 * 2^23 + x, minus
+      // 1.5 * 2^23; then times the key's scale
+      const float* ks = ksm + es * BN;
+      const float2 nmag = make_float2(-kMagic, -kMagic);
 #pragma unroll
-      for (int i = 0; i < HC; i += 4) {
+      for (int i = 0; i < BN; i += 4) {
         const float4 k4 = *reinterpret_cast<const float4*>(ks + i);
-        const float x0 = i2f_exact(u[i]) - kMagic, x1 = i2f_exact(u[i + 1]) - kMagic;
-        const float x2 = i2f_exact(u[i + 2]) - kMagic, x3 = i2f_exact(u[i + 3]) - kMagic;
-        const f2 a = fmul2(fmul2(pack_f2(x0, x1), pack_f2(k4.x, k4.y)), c22);
-        const f2 c = fmul2(fmul2(pack_f2(x2, x3), pack_f2(k4.z, k4.w)), c22);
-        unpack_f2(a, s[i], s[i + 1]);
-        unpack_f2(c, s[i + 2], s[i + 3]);
+        float2 a = __fadd2_rn(make_float2(i2f_exact(__float_as_uint(s[i])), i2f_exact(__float_as_uint(s[i + 1]))), nmag);
+        float2 c = __fadd2_rn(make_float2(i2f_exact(__float_as_uint(s[i + 2])), i2f_exact(__float_as_uint(s[i + 3]))), nmag);
+        a = __fmul2_rn(a, make_float2(k4.x, k4.y));
+        c = __fmul2_rn(c, make_float2(k4.z, k4.w));
+        s[i] = a.x;
+        s[i + 1] = a.y;
+        s[i + 2] = c.x;
+        s[i + 3] = c.y;
       }
     } else if (MODE == kCompat) {
       // the reference's rule: q.k_msb * sm_scale, plus q.k_lsb * sm_scale
       // where the criterion tile's largest q.k_msb * sm_scale is below tile_thr
       const float sc = p.sm_scale, thr = p.tile_thr;
       const int lim_n = p.N - n0;
-      bool hot = false;
+      bool hlo = false, hhi = false;
 #pragma unroll
-      for (int i = 0; i < HC; ++i) {
-        s[i] = __uint_as_float(u[i]) * sc;
-        hot |= (i < lim_n) && s[i] >= thr;
+      for (int i = 0; i < BN; ++i) {
+        s[i] = s[i] * sc;
+        const bool hot = (i < lim_n) && s[i] >= thr;
+        if (i < 32) hlo |= hot;
+        else hhi |= hot;
       }
-      if (!compat_vote(valid && hot, tt)) {
+      bool any_lo, any_hi;
+      compat_vote(valid && hlo, valid && hhi, tt, any_lo, any_hi);
 #pragma unroll
-        for (int i = 0; i < HC; ++i) s[i] = s[i] + __uint_as_float(lr[i]) * sc;
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        float lr[32];
+        tmem_ld32f(tl + sb * L::kSW + BN + 32 * hlf, lr);
+        tmem_wait_ld();
+        if (!(hlf ? any_hi : any_lo)) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[32 * hlf + i] = s[32 * hlf + i] + lr[i] * sc;
+        }
       }
-#pragma unroll
-      for (int i = 0; i < HC; ++i) s[i] *= kLog2e;
-    } else {
-#pragma unroll
-      for (int i = 0; i < HC; ++i) s[i] = __uint_as_float(u[i]) * c2;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b.s_empty[sb]);
     }
-    if (key_bias) {
+    if (prescale) {
+      const float* kb = kbm + es * BN;  // key bias * log2 e (zeros without one)
 #pragma unroll
-      for (int i = 0; i < HC; i += 4) {
+      for (int i = 0; i < BN; i += 4) {
         const float4 k4 = *reinterpret_cast<const float4*>(kb + i);
-        s[i] += k4.x;
-        s[i + 1] += k4.y;
-        s[i + 2] += k4.z;
-        s[i + 3] += k4.w;
+        s[i] = fmaf(s[i], cs, k4.x);
+        s[i + 1] = fmaf(s[i + 1], cs, k4.y);
+        s[i + 2] = fmaf(s[i + 2], cs, k4.z);
+        s[i + 3] = fmaf(s[i + 3], cs, k4.w);
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&b.k_empty[es]);
     if (gen_bias && valid) {
-      for (int i = 0; i < HC; ++i)
+      for (int i = 0; i < BN; ++i)
         if (n0 + i < p.N) s[i] += __ldg(brow + (int64_t)(n0 + i) * p.b_sn) * kLog2e;
     }
     // keys past N and, with the causal mask, keys after the row's diagonal:
     // only tiles that reach them pay for the per-element test
     const int lim = min(p.N, klim) - n0;
-    if (lim < HC) {
+    if (lim < BN) {
 #pragma unroll
-      for (int i = 0; i < HC; ++i)
+      for (int i = 0; i < BN; ++i)
         if (i >= lim) s[i] = -INFINITY;
     }
   };
 
-  // Online statistics of this thread's half row over one tile (four
-  // independent max / sum chains).
-  auto stats = [&](const float (&s)[HC], float& m, float& l) {
-    float mx[4];
+  // Online statistics (log2 domain) of the row over one tile.
+  auto stats = [&](const float (&s)[BN], float& m, float& l) {
+    static_assert(BN % 8 == 0, "max tree over 8-column groups");
+    float a0 = fmaxf(s[0], s[1]), a1 = fmaxf(s[2], s[3]), a2 = fmaxf(s[4], s[5]), a3 = fmaxf(s[6], s[7]);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) mx[k] = s[k];
-#pragma unroll
-    for (int i = 4; i < HC; i += 4)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) mx[k] = fmaxf(mx[k], s[i + k]);
-    const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-    const float mn = fmaxf(m, tmax);
+    for (int i = 8; i < BN; i += 8) {
+      a0 = fmax3(a0, s[i], s[i + 1]);
+      a1 = fmax3(a1, s[i + 2], s[i + 3]);
+      a2 = fmax3(a2, s[i + 4], s[i + 5]);
+      a3 = fmax3(a3, s[i + 6], s[i + 7]);
+    }
+    const float mn = fmaxf(m, fmax3(fmaxf(a0, a1), a2, a3) * cse);
     if (mn == -INFINITY) return;
-    const f2 nm2 = pack_f2(-mn, -mn);
-    f2 acc[2];
+    const float2 c2v = make_float2(cse, cse), nm = make_float2(-mn, -mn);
+    float2 acc[4];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      float a0, a1;
-      unpack_f2(fadd2(pack_f2(s[2 * k], s[2 * k + 1]), nm2), a0, a1);
-      acc[k] = pack_f2(fast_exp2(a0), fast_exp2(a1));
-    }
+    for (int k = 0; k < 4; ++k) acc[k] = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int i = 4; i < HC; i += 4)
+    for (int i = 0; i < BN; i += 8) {
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        float a0, a1;
-        unpack_f2(fadd2(pack_f2(s[i + 2 * k], s[i + 2 * k + 1]), nm2), a0, a1);
-        acc[k] = fadd2(acc[k], pack_f2(fast_exp2(a0), fast_exp2(a1)));
+      for (int k = 0; k < 4; ++k) {
+        const float2 x = __ffma2_rn(make_float2(s[i + 2 * k], s[i + 2 * k + 1]), c2v, nm);
+        acc[k] = __fadd2_rn(acc[k], make_float2(exp2_split(x.x, k), exp2_split(x.y, k)));
       }
-    float t0, t1, t2, t3;
-    unpack_f2(acc[0], t0, t1);
-    unpack_f2(acc[1], t2, t3);
-    l = l * fast_exp2(m - mn) + ((t0 + t1) + (t2 + t3));
-    m = mn;
-  };
-
-  // Both softmax threads of a row end up with the statistics of the whole
-  // row: half 0 then half 1, in that order, on both threads.
-  auto combine = [&](float& m, float& l) {
-    stm[(0 * 2 + hf) * BM + r] = m;
-    stm[(1 * 2 + hf) * BM + r] = l;
-    named_sync(1, kSoftThreads);
-    const float ma = stm[(0 * 2 + 0) * BM + r], la = stm[(1 * 2 + 0) * BM + r];
-    const float mb = stm[(0 * 2 + 1) * BM + r], lb = stm[(1 * 2 + 1) * BM + r];
-    named_sync(1, kSoftThreads);
-    const float mn = fmaxf(ma, mb);
-    if (mn == -INFINITY) {
-      m = mn;
-      l = 0.f;
-      return;
     }
+    const float2 a = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+    l = l * fast_exp2(m - mn) + (a.x + a.y);
     m = mn;
-    l = la * fast_exp2(ma - mn) + lb * fast_exp2(mb - mn);
   };
 
   const bool want_tok = p.tok_partial != nullptr;
   float* tokp = want_tok ? p.tok_partial + (((int64_t)z * p.H + h) * p.mtiles + mt) * p.N : nullptr;
-  // column sums of tile pair pi (128 keys) from TMEM; warps of half 0 cover
-  // the 128 lanes = keys
+  // column sums of tile pair pi (128 keys) from TMEM: lane = key
   auto read_pair = [&](int pi) {
     const int cb = pi & 1;
     if (!alive) return;
@@ -787,11 +830,11 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&b.cs_empty[cb]);
-    const int key = pi * 2 * BN + qd * 32 + lane;
+    const int key = pi * 2 * BN + warp * 32 + lane;
     if (key < p.N && key < nt * BN) tokp[key] = __uint_as_float(v);
   };
 
-  float s[HC];
+  float s[BN];
   float m_run = -INFINITY, l_run = 0.f;  // statistics of the scores in use
   float mf = -INFINITY, lf = 0.f;        // statistics of the full score (pass 1b)
   bool flag = false, warp_any = false;
@@ -800,12 +843,12 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
   int32_t* dump = (MODE == kQuant && p.score_out)
                       ? p.score_out + ((int64_t)z * p.H + h) * ((p.M + p.score_rs - 1) / p.score_rs) * (int64_t)p.N
                       : nullptr;
-  f2 inv2 = pack_f2(0.f, 0.f), mn2 = pack_f2(0.f, 0.f);
-  // Count V prune (VC): this thread's kMaxVPruneCount smallest (score, key)
-  // pairs of the scores its row ends up using, ascending in (score, key), in
-  // this thread's column of a shared-memory list (the largest entry cached in
-  // a register, so a score that does not enter the list costs one compare);
-  // the row's v_count-th smallest pair (kvs, kvn) then marks the keys to drop.
+  float mo = -INFINITY;  // pass 2: P = exp2(s * cse + mo)
+  // Count V prune (VC): this row's kMaxVPruneCount smallest (score, key)
+  // pairs of the scores it ends up using, ascending in (score, key), in this
+  // thread's column of a shared-memory list (the largest entry cached in a
+  // register, so a score that does not enter the list costs one compare);
+  // the row's v_count-th smallest pair (kvs, kvn) marks the keys to drop.
   constexpr int KC = kMaxVPruneCount;
   float* lv = reinterpret_cast<float*>(sm + L::oCv);
   int* ln = reinterpret_cast<int*>(sm + L::oCv + KC * kSoftThreads * 4);
@@ -821,10 +864,10 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
     cmax = INFINITY;
   };
   auto track = [&](int j) {
-    const int n0 = j * BN + c0;
+    const int n0 = j * BN;
     const int lim = p.N - n0;  // keys past N are not part of the row
 #pragma unroll
-    for (int i = 0; i < HC; ++i) {
+    for (int i = 0; i < BN; ++i) {
       const float x = s[i];
       // keys arrive in increasing order, so an equal score ranks after the
       // entries already kept: only a smaller score enters the list
@@ -846,23 +889,21 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
   int pairs_read = 0;
   const int npairs = (nt + 1) / 2;
   // One loop over the passes keeps a single copy of the tile code:
-  //   pass 0 statistics of the MSB (QUANT) / only (DENSE) score
+  //   pass 0 statistics of the MSB (QUANT) / only (DENSE, COMPAT) score
   //   pass 1 statistics of the full score of refetched rows (QUANT, if any)
   //   pass 2 P, V prune, P -> shared memory (P.V and the column sums run on
   //          the tensor cores)
   for (int pass = 0; pass < 3; ++pass) {
     if (pass == 1) {
-      combine(m_run, l_run);
       // ---- decide the refetch, build Q'
       if (MODE == kQuant) {
         flag = alive && valid && __frcp_rn(l_run) < p.refetch_thr;
         if (VC && flag) track_reset();  // a refetched row ends up using its full scores
-        // Q' bytes [D, 2D): q8 for a refetched row, zeros otherwise (each
-        // thread of the row copies half of the chunks)
+        // Q' bytes [D, 2D): q8 for a refetched row, zeros otherwise
         uint8_t* base = sm + L::oQ;
         const int sw = r & 7;
 #pragma unroll
-        for (int c = hf * (D / 32); c < (hf + 1) * (D / 32); ++c) {
+        for (int c = 0; c < D / 16; ++c) {
           const int src_off = 16 * c, dst_off = D + 16 * c;
           const uint4 v = *reinterpret_cast<const uint4*>(base + (src_off >> 7) * (BM * 128) + r * 128 +
                                                           ((((src_off >> 4) & 7) ^ sw) << 4));
@@ -880,7 +921,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
             : "memory");
         any = (int)anyv;
         if (tid == 0) *decision = any;
-        if (p.refetch_out && valid && hf == 0) p.refetch_out[((int64_t)z * p.H + h) * p.M + row] = flag;
+        if (p.refetch_out && valid) p.refetch_out[((int64_t)z * p.H + h) * p.M + row] = flag;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(b.dec_ready);
@@ -888,34 +929,15 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
       warp_any = __any_sync(0xffffffffu, flag);
     }
     if (pass == 2) {
-      if (MODE == kQuant && any) {
-        combine(mf, lf);
-        if (flag) {
-          m_run = mf;
-          l_run = lf;
-        }
+      if (MODE == kQuant && any && flag) {
+        m_run = mf;
+        l_run = lf;
       }
-      const float inv_l = (valid && m_run != -INFINITY && l_run > 0.f) ? 1.f / l_run : 0.f;
-      const float mneg = (m_run == -INFINITY) ? 0.f : -m_run;
-      inv2 = pack_f2(inv_l, inv_l);
-      mn2 = pack_f2(mneg, mneg);
-      if (VC) {
-        // merge the row's two half-row lists up to the v_count-th smallest
-        // (score, key); both threads of the row find the same pair
-        named_sync(1, kSoftThreads);
-        const int ta = tid & (kSoftThreads / 2 - 1), tb = ta + kSoftThreads / 2;
-        int ia = 0, ib = 0;
-        for (int q = 0; q < p.v_count; ++q) {
-          const float xa = ia < KC ? lv[ia * kSoftThreads + ta] : INFINITY;
-          const float xb = ib < KC ? lv[ib * kSoftThreads + tb] : INFINITY;
-          const int ya = ia < KC ? ln[ia * kSoftThreads + ta] : INT_MAX;
-          const int yb = ib < KC ? ln[ib * kSoftThreads + tb] : INT_MAX;
-          const bool pa = xa < xb || (xa == xb && ya < yb);
-          kvs = pa ? xa : xb;
-          kvn = pa ? ya : yb;
-          ia += pa ? 1 : 0;
-          ib += pa ? 0 : 1;
-        }
+      mo = (valid && m_run != -INFINITY && l_run > 0.f) ? -(m_run + __log2f(l_run)) : -INFINITY;
+      if (VC && p.v_count > 0) {
+        // the list is ascending: its v_count-th entry marks the keys to drop
+        kvs = lv[(p.v_count - 1) * kSoftThreads + tid];
+        kvn = ln[(p.v_count - 1) * kSoftThreads + tid];
       }
     }
     for (int j = 0; j < nt; ++j) {
@@ -939,39 +961,45 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
       // ---- pass 2 tile
       const int pb = j % kNP;
       if (alive) {
-        uint32_t drop = 0;  // count V prune: keys at or below (kvs, kvn)
+        uint64_t drop = 0;  // count V prune: keys at or below (kvs, kvn)
         if (VC) {
-          const int n0 = j * BN + c0;
+          const int n0 = j * BN;
 #pragma unroll
-          for (int i = 0; i < HC; ++i)
-            drop |= (uint32_t)(s[i] < kvs || (s[i] == kvs && n0 + i <= kvn)) << i;
+          for (int i = 0; i < BN; ++i)
+            drop |= (uint64_t)(s[i] < kvs || (s[i] == kvs && n0 + i <= kvn)) << i;
         }
+        const float2 c2v = make_float2(cse, cse), mo2 = make_float2(mo, mo);
 #pragma unroll
-        for (int i = 0; i < HC; i += 2) {
-          float a0, a1;
-          unpack_f2(fadd2(pack_f2(s[i], s[i + 1]), mn2), a0, a1);
-          unpack_f2(fmul2(pack_f2(fast_exp2(a0), fast_exp2(a1)), inv2), s[i], s[i + 1]);
+        for (int i = 0; i < BN; i += 2) {
+          const float2 x = __ffma2_rn(make_float2(s[i], s[i + 1]), c2v, mo2);
+          s[i] = exp2_split(x.x, (i >> 1) & 3);
+          s[i + 1] = exp2_split(x.y, (i >> 1) & 3);
         }
         if (vthr > 0.f) {
 #pragma unroll
-          for (int i = 0; i < HC; ++i) s[i] = s[i] < vthr ? 0.f : s[i];
+          for (int i = 0; i < BN; i += 2) {
+            const float2 k = make_float2(ge_one(s[i], vthr), ge_one(s[i + 1], vthr));
+            const float2 q = __fmul2_rn(make_float2(s[i], s[i + 1]), k);
+            s[i] = q.x;
+            s[i + 1] = q.y;
+          }
         }
         if (VC) {
 #pragma unroll
-          for (int i = 0; i < HC; ++i) s[i] = (drop >> i) & 1u ? 0.f : s[i];
+          for (int i = 0; i < BN; ++i) s[i] = (drop >> i) & 1u ? 0.f : s[i];
         }
         // P -> shared memory: A operand of P.V (K-major) and, read as an
         // MN-major operand, of the column sums; 128B swizzle
         if (mbar_wait(&b.p_empty[pb], ((j / kNP) & 1) ^ 1, kErrSoftmax | 3, abort)) {
           uint8_t* prow = sm + L::oP + pb * L::kPBytes + r * 128;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 8; ++c) {
             uint4 v;
             v.x = pack2<T>(s[8 * c], s[8 * c + 1]);
             v.y = pack2<T>(s[8 * c + 2], s[8 * c + 3]);
             v.z = pack2<T>(s[8 * c + 4], s[8 * c + 5]);
             v.w = pack2<T>(s[8 * c + 6], s[8 * c + 7]);
-            *reinterpret_cast<uint4*>(prow + (((hf * 4 + c) ^ (r & 7)) << 4)) = v;
+            *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = v;
           }
           fence_proxy_async_smem();
           __syncwarp();
@@ -981,35 +1009,33 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
         }
       }
       // column sums of the pair before last (its MMA had a pair's time to finish)
-      if (want_tok && hf == 0 && (j & 1) && j >= 3) read_pair(pairs_read++);
+      if (want_tok && (j & 1) && j >= 3) read_pair(pairs_read++);
     }
   }
-  if (want_tok && hf == 0)
+  if (want_tok)
     while (pairs_read < npairs) read_pair(pairs_read++);
   if (want_tok)  // skipped key tiles: no probability reached them
     for (int key = nt * BN + tid; key < p.N; key += kSoftThreads) tokp[key] = 0.f;
 
-  // ---- epilogue: O (already normalised) from TMEM, this thread's half row
+  // ---- epilogue: O (already normalised) from TMEM, this thread's row
   if (!mbar_wait(b.o_full, 0, kErrSoftmax | 4, abort)) alive = false;
   tc_fence_after();
   float asum = 0.f;
   const int hslot = p.out_head_map ? p.out_head_map[h] : h;
   const bool out_ok = hslot >= 0 && hslot < p.out_head_slots;
-  T* orow = static_cast<T*>(p.out) + (int64_t)z * p.o_sz + (int64_t)hslot * p.o_sh + (int64_t)row * p.o_sm +
-            hf * (D / 2);
+  T* orow = static_cast<T*>(p.out) + (int64_t)z * p.o_sz + (int64_t)hslot * p.o_sh + (int64_t)row * p.o_sm;
   const bool out16 = (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
 #pragma unroll
-  for (int c = 0; c < D / 64; ++c) {
-    uint32_t o[32];
-    tmem_ld32(tl + L::kColO + hf * (D / 2) + 32 * c, o);
+  for (int c = 0; c < D / 32; ++c) {
+    float o[32];
+    tmem_ld32f(tl + L::kColO + 32 * c, o);
     tmem_wait_ld();
     if (alive && valid) {
       uint32_t pk[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float x0 = __uint_as_float(o[2 * i]), x1 = __uint_as_float(o[2 * i + 1]);
-        asum += fabsf(x0) + fabsf(x1);
-        pk[i] = pack2<T>(x0, x1);
+        asum += fabsf(o[2 * i]) + fabsf(o[2 * i + 1]);
+        pk[i] = pack2<T>(o[2 * i], o[2 * i + 1]);
       }
       if (out_ok) {
         if (out16) {

@@ -65,7 +65,10 @@ def _pool_map(fn, items):
 
 
 def _np(t):
-    return t.detach().cpu().numpy()
+    t = t.detach()
+    if t.dtype in (torch.bfloat16, torch.float16):
+        t = t.float()  # numpy has no bf16
+    return t.cpu().numpy()
 
 
 def _chunk(n_keys):
