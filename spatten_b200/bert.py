@@ -67,9 +67,13 @@ def slice_linear_weights(linear_layer, active_indices, num_heads, head_dim):
     return gather_head_rows(w, active_indices, head_dim), gather_head_rows(b, active_indices, head_dim)
 
 
-def _mask_bias(attention_mask, B, S):
+def _mask_bias(attention_mask, B, S, per_key=True):
     """HF mask as passed to the attention module -> additive bias view, or None.
-    Float masks are additive (eager); bool masks mark kept keys (sdpa)."""
+    Float masks are additive (eager); bool masks mark kept keys (sdpa). An
+    encoder's mask is a key (padding) mask repeated over the query rows, so
+    with ``per_key`` a [B, 1, Sq, Sk] mask is read from its first row: the
+    kernel then stages it per key tile instead of loading a bias per score
+    (HF materialises the full mask, e.g. while a CUDA graph is captured)."""
     if attention_mask is None:
         return None
     m = attention_mask
@@ -77,6 +81,8 @@ def _mask_bias(attention_mask, B, S):
         m = m[:, None, None, :].to(torch.bool) if m.dtype != torch.bool else m[:, None, None, :]
     if m.dim() == 3:
         m = m[:, None]
+    if per_key and m.dim() == 4 and m.shape[2] > 1:
+        m = m[:, :, :1, :]
     if m.dtype == torch.bool:
         return torch.zeros(m.shape, dtype=torch.float32, device=m.device).masked_fill_(
             ~m, torch.finfo(torch.float32).min)
@@ -166,7 +172,7 @@ class SpattenBertSelfAttention(BertSelfAttention):
             q = qkv4[:, :, 0].permute(0, 2, 1, 3)          # [B, cur, S, d] strided views
             k = qkv4[:, :, 1].permute(0, 2, 1, 3)
             v = qkv4[:, :, 2].permute(0, 2, 1, 3)
-        bias = _mask_bias(attention_mask, B, S)
+        bias = _mask_bias(attention_mask, B, S, per_key=not getattr(self, "is_decoder", False))
         v_thr, v_count = 0.0, 0
         if self.enable_v_prune:
             if self.v_prune_threshold is not None:

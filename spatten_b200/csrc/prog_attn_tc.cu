@@ -108,11 +108,7 @@ struct Layout {
   static constexpr int kNumBars = 2 * kNStg + 2 * kNExp + 2 * 2 + 2 * kNP + 2 * kNV + 2 * 2 + 3 + 8;
   static constexpr int oTmem = oBar + kNumBars * 8;
   static constexpr int oFlag = oTmem + 4;  // int abort, int decision, int key tiles of the CTA
-  // count V prune (VC): each softmax thread's kMaxVPruneCount smallest
-  // (score, key) pairs, float [kMaxVPruneCount][kSoftThreads] then int [..]
-  static constexpr int oCv = (oFlag + 16 + 15) & ~15;
-  static constexpr int kCvBytes = VC ? 2 * kMaxVPruneCount * kSoftThreads * 4 : 0;
-  static constexpr int kBytes = oCv + kCvBytes;
+  static constexpr int kBytes = oFlag + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
@@ -581,35 +577,6 @@ SPATTEN_DEV float fmax3(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
-// 2^x for x <= 0 on the FMA pipe instead of the MUFU (Cody-Waite range
-// reduction: x = n + f with n = rint(x), f in [-1/2, 1/2]; 2^f by the Taylor
-// series of exp(f ln 2) to degree 6: relative error below 2.5e-7 in fp32
-// (1.6e-7 from the series); 2^n added to the exponent field). Inputs below -127 (and -inf)
-// give 0 or a subnormal below 6e-39. Part of a tile's exponentials go here
-// so that the MUFU and the FMA pipe share them.
-SPATTEN_DEV float exp2_fma(float x) {
-  constexpr float kRnd = 12582912.0f;  // 1.5 * 2^23: x + kRnd rounds x to an integer
-  const float xc = fmaxf(x, -127.0f);
-  const float j = xc + kRnd;
-  const float f = xc - (j - kRnd);
-  // (ln 2)^k / k!, k = 6 .. 1
-  float p = 1.5403530393381608e-4f;
-  p = fmaf(p, f, 1.3333558146428443e-3f);
-  p = fmaf(p, f, 9.6181291076284772e-3f);
-  p = fmaf(p, f, 5.5504108664821580e-2f);
-  p = fmaf(p, f, 2.4022650695910071e-1f);
-  p = fmaf(p, f, 6.9314718055994531e-1f);
-  p = fmaf(p, f, 1.0f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
-}
-#ifndef SPATTEN_TC_FMA_EXP
-#define SPATTEN_TC_FMA_EXP 0
-#endif
-// which of the four exponential chains of a tile run on the FMA pipe
-SPATTEN_DEV float exp2_split(float x, int chain) {
-  return (SPATTEN_TC_FMA_EXP && chain == 3) ? exp2_fma(x) : fast_exp2(x);
-}
-
 // 1.0f if a >= b, else 0.0f
 SPATTEN_DEV float ge_one(float a, float b) {
   float d;
@@ -761,13 +728,16 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
     }
     if (prescale) {
       const float* kb = kbm + es * BN;  // key bias * log2 e (zeros without one)
+      const float2 cs2 = make_float2(cs, cs);
 #pragma unroll
       for (int i = 0; i < BN; i += 4) {
         const float4 k4 = *reinterpret_cast<const float4*>(kb + i);
-        s[i] = fmaf(s[i], cs, k4.x);
-        s[i + 1] = fmaf(s[i + 1], cs, k4.y);
-        s[i + 2] = fmaf(s[i + 2], cs, k4.z);
-        s[i + 3] = fmaf(s[i + 3], cs, k4.w);
+        const float2 a = __ffma2_rn(make_float2(s[i], s[i + 1]), cs2, make_float2(k4.x, k4.y));
+        const float2 c = __ffma2_rn(make_float2(s[i + 2], s[i + 3]), cs2, make_float2(k4.z, k4.w));
+        s[i] = a.x;
+        s[i + 1] = a.y;
+        s[i + 2] = c.x;
+        s[i + 3] = c.y;
       }
     }
     __syncwarp();
@@ -808,7 +778,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const float2 x = __ffma2_rn(make_float2(s[i + 2 * k], s[i + 2 * k + 1]), c2v, nm);
-        acc[k] = __fadd2_rn(acc[k], make_float2(exp2_split(x.x, k), exp2_split(x.y, k)));
+        acc[k] = __fadd2_rn(acc[k], make_float2(fast_exp2(x.x), fast_exp2(x.y)));
       }
     }
     const float2 a = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
@@ -845,43 +815,43 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
                       : nullptr;
   float mo = -INFINITY;  // pass 2: P = exp2(s * cse + mo)
   // Count V prune (VC): this row's kMaxVPruneCount smallest (score, key)
-  // pairs of the scores it ends up using, ascending in (score, key), in this
-  // thread's column of a shared-memory list (the largest entry cached in a
-  // register, so a score that does not enter the list costs one compare);
-  // the row's v_count-th smallest pair (kvs, kvn) marks the keys to drop.
-  constexpr int KC = kMaxVPruneCount;
-  float* lv = reinterpret_cast<float*>(sm + L::oCv);
-  int* ln = reinterpret_cast<int*>(sm + L::oCv + KC * kSoftThreads * 4);
-  float cmax = INFINITY;
+  // pairs of the scores it ends up using, ascending in (score, key), in
+  // registers (the count-prune instantiation runs one CTA per SM with the
+  // register budget for it); the row's v_count-th smallest pair (kvs, kvn)
+  // marks the keys to drop.
+  constexpr int KC = VC ? kMaxVPruneCount : 1;
+  float cv[KC];
+  int cn[KC];
   float kvs = -INFINITY;
   int kvn = -1;
   auto track_reset = [&]() {
 #pragma unroll
     for (int q = 0; q < KC; ++q) {
-      lv[q * kSoftThreads + tid] = INFINITY;
-      ln[q * kSoftThreads + tid] = INT_MAX;
+      cv[q] = INFINITY;
+      cn[q] = INT_MAX;
     }
-    cmax = INFINITY;
   };
   auto track = [&](int j) {
     const int n0 = j * BN;
     const int lim = p.N - n0;  // keys past N are not part of the row
 #pragma unroll
     for (int i = 0; i < BN; ++i) {
-      const float x = s[i];
       // keys arrive in increasing order, so an equal score ranks after the
-      // entries already kept: only a smaller score enters the list
-      if (i < lim && x < cmax) {
-        int q = KC - 1;
-        for (; q > 0; --q) {
-          const float y = lv[(q - 1) * kSoftThreads + tid];
-          if (!(y > x)) break;
-          lv[q * kSoftThreads + tid] = y;
-          ln[q * kSoftThreads + tid] = ln[(q - 1) * kSoftThreads + tid];
+      // entries already kept: only a smaller score enters the list, which
+      // then bubbles into place
+      float x = s[i];
+      if (i < lim && x < cv[KC - 1]) {
+        int xn = n0 + i;
+#pragma unroll
+        for (int q = 0; q < KC; ++q) {
+          const bool lt = x < cv[q];
+          const float tv = cv[q];
+          const int tn = cn[q];
+          cv[q] = lt ? x : tv;
+          cn[q] = lt ? xn : tn;
+          x = lt ? tv : x;
+          xn = lt ? tn : xn;
         }
-        lv[q * kSoftThreads + tid] = x;
-        ln[q * kSoftThreads + tid] = n0 + i;
-        cmax = lv[(KC - 1) * kSoftThreads + tid];
       }
     }
   };
@@ -936,8 +906,12 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
       mo = (valid && m_run != -INFINITY && l_run > 0.f) ? -(m_run + __log2f(l_run)) : -INFINITY;
       if (VC && p.v_count > 0) {
         // the list is ascending: its v_count-th entry marks the keys to drop
-        kvs = lv[(p.v_count - 1) * kSoftThreads + tid];
-        kvn = ln[(p.v_count - 1) * kSoftThreads + tid];
+#pragma unroll
+        for (int q = 0; q < KC; ++q)
+          if (q == p.v_count - 1) {
+            kvs = cv[q];
+            kvn = cn[q];
+          }
       }
     }
     for (int j = 0; j < nt; ++j) {
@@ -972,8 +946,8 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
 #pragma unroll
         for (int i = 0; i < BN; i += 2) {
           const float2 x = __ffma2_rn(make_float2(s[i], s[i + 1]), c2v, mo2);
-          s[i] = exp2_split(x.x, (i >> 1) & 3);
-          s[i + 1] = exp2_split(x.y, (i >> 1) & 3);
+          s[i] = fast_exp2(x.x);
+          s[i + 1] = fast_exp2(x.y);
         }
         if (vthr > 0.f) {
 #pragma unroll

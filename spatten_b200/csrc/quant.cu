@@ -120,22 +120,33 @@ __global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict
   const int lane = threadIdx.x & 31, sub = lane / LPR, li = lane % LPR;
   const int64_t rows = (int64_t)Z * H * M;
   const int64_t step = (int64_t)gridDim.x * (blockDim.x >> 5) * RPW;
-  for (int64_t r0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW; r0 < rows;
-       r0 += step) {
-    const int64_t r = r0 + sub;
-    const bool live = r < rows;
-    float v[EPL];
-    if (live) {
+  // this lane's two 16-byte chunks of row r (zeros past the end)
+  auto load = [&](int64_t r, uint4 (&raw)[2]) {
+    if (r < rows) {
       int64_t m, h, z;
       row_coords(r, M, H, m, h, z);
       const uint4* src = reinterpret_cast<const uint4*>(x + z * sz + h * sh + m * sm) + 2 * li;
-      const uint4 raw[2] = {__ldg(src), __ldg(src + 1)};
+      raw[0] = __ldg(src);
+      raw[1] = __ldg(src + 1);
+    } else {
+      raw[0] = raw[1] = make_uint4(0, 0, 0, 0);
+    }
+  };
+  const int64_t first = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW;
+  uint4 nxt[2];
+  load(first + sub, nxt);
+  // the next step's rows are loaded before this step's are quantised: two
+  // steps of loads in flight per lane
+  for (int64_t r0 = first; r0 < rows; r0 += step) {
+    const int64_t r = r0 + sub;
+    const bool live = r < rows;
+    const uint4 raw[2] = {nxt[0], nxt[1]};
+    load(r0 + step + sub, nxt);
+    float v[EPL];
+    {
       const T* e = reinterpret_cast<const T*>(raw);
 #pragma unroll
       for (int i = 0; i < EPL; ++i) v[i] = to_f32<T>(e[i]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < EPL; ++i) v[i] = 0.f;
     }
     float amax = 0.f;
 #pragma unroll
