@@ -54,6 +54,10 @@ constexpr int BN = 64;         // keys per tile
 constexpr int kSoftWarps = 4;  // one thread per query row, all 64 columns of a tile
 constexpr int kSoftThreads = kSoftWarps * 32;
 // Expander warps (64 / 32 keys of a 64-key tile per thread).
+#ifndef SPATTEN_TC_KS_CHUNK
+#define SPATTEN_TC_KS_CHUNK 64
+#endif
+constexpr int kKsChunk = SPATTEN_TC_KS_CHUNK;  // key-scale columns read per fenced chunk
 #ifndef SPATTEN_TC_EXP_WARPS
 #define SPATTEN_TC_EXP_WARPS 2
 #endif
@@ -113,22 +117,22 @@ struct Layout {
 };
 
 struct Bars {
-  uint64_t* stg_full;
-  uint64_t* stg_empty;
-  uint64_t* k_full;
-  uint64_t* k_empty;
-  uint64_t* s_full;
-  uint64_t* s_empty;
-  uint64_t* p_full;
-  uint64_t* p_empty;
-  uint64_t* v_full;
-  uint64_t* v_empty;
-  uint64_t* cs_full;
-  uint64_t* cs_empty;
-  uint64_t* q_ready;
-  uint64_t* dec_ready;
-  uint64_t* o_full;
-  uint64_t* vote;  // [2 buffers][4 vote groups] (COMPAT)
+  SBarArr stg_full;
+  SBarArr stg_empty;
+  SBarArr k_full;
+  SBarArr k_empty;
+  SBarArr s_full;
+  SBarArr s_empty;
+  SBarArr p_full;
+  SBarArr p_empty;
+  SBarArr v_full;
+  SBarArr v_empty;
+  SBarArr cs_full;
+  SBarArr cs_empty;
+  SBar q_ready;
+  SBar dec_ready;
+  SBar o_full;
+  SBarArr vote;  // [2 buffers][4 vote groups] (COMPAT)
 };
 
 // Pairs of fp32 values for the packed (f32x2) FP instructions of sm_100.
@@ -170,23 +174,28 @@ struct Cta {
   int z, h, kvh, mt, m0, nt;
 
   SPATTEN_DEV Cta(const TcParams& pp, uint8_t* base) : P(pp), p(pp.a), sm(base) {
-    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::oBar);
-    b.stg_full = bar; bar += kNStg;
-    b.stg_empty = bar; bar += kNStg;
-    b.k_full = bar; bar += kNExp;
-    b.k_empty = bar; bar += kNExp;
-    b.s_full = bar; bar += 2;
-    b.s_empty = bar; bar += 2;
-    b.p_full = bar; bar += kNP;
-    b.p_empty = bar; bar += kNP;
-    b.v_full = bar; bar += kNV;
-    b.v_empty = bar; bar += kNV;
-    b.cs_full = bar; bar += 2;
-    b.cs_empty = bar; bar += 2;
-    b.q_ready = bar++;
-    b.dec_ready = bar++;
-    b.o_full = bar++;
-    b.vote = bar; bar += 8;
+    uint32_t bar = smem_u32(sm + L::oBar);
+    auto take = [&](int n) {
+      const SBarArr r{bar};
+      bar += 8u * (uint32_t)n;
+      return r;
+    };
+    b.stg_full = take(kNStg);
+    b.stg_empty = take(kNStg);
+    b.k_full = take(kNExp);
+    b.k_empty = take(kNExp);
+    b.s_full = take(2);
+    b.s_empty = take(2);
+    b.p_full = take(kNP);
+    b.p_empty = take(kNP);
+    b.v_full = take(kNV);
+    b.v_empty = take(kNV);
+    b.cs_full = take(2);
+    b.cs_empty = take(2);
+    b.q_ready = take(1)[0];
+    b.dec_ready = take(1)[0];
+    b.o_full = take(1)[0];
+    b.vote = take(8);
     abort = reinterpret_cast<volatile int*>(sm + L::oFlag);
     decision = reinterpret_cast<int*>(sm + L::oFlag + 4);
     // With a causal mask or key limits the work grows with the row index:
@@ -225,32 +234,32 @@ struct Cta {
 
   SPATTEN_DEV void init_barriers() {
     for (int i = 0; i < kNStg; ++i) {
-      mbar_init(&b.stg_full[i], 1);
-      mbar_init(&b.stg_empty[i], kExpWarps);
+      mbar_init(b.stg_full[i], 1);
+      mbar_init(b.stg_empty[i], kExpWarps);
     }
     for (int i = 0; i < kNExp; ++i) {
-      mbar_init(&b.k_full[i], MODE == kQuant ? kExpWarps : 1 + kExpWarps);
-      mbar_init(&b.k_empty[i], 1 + kSoftWarps);
+      mbar_init(b.k_full[i], MODE == kQuant ? kExpWarps : 1 + kExpWarps);
+      mbar_init(b.k_empty[i], 1 + kSoftWarps);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&b.s_full[i], 1);
-      mbar_init(&b.s_empty[i], kSoftWarps);
-      mbar_init(&b.cs_full[i], 1);
-      mbar_init(&b.cs_empty[i], 4);
+      mbar_init(b.s_full[i], 1);
+      mbar_init(b.s_empty[i], kSoftWarps);
+      mbar_init(b.cs_full[i], 1);
+      mbar_init(b.cs_empty[i], 4);
     }
     for (int i = 0; i < kNP; ++i) {
-      mbar_init(&b.p_full[i], kSoftWarps);
-      mbar_init(&b.p_empty[i], 1);
+      mbar_init(b.p_full[i], kSoftWarps);
+      mbar_init(b.p_empty[i], 1);
     }
     for (int i = 0; i < kNV; ++i) {
-      mbar_init(&b.v_full[i], 1);
-      mbar_init(&b.v_empty[i], 1);
+      mbar_init(b.v_full[i], 1);
+      mbar_init(b.v_empty[i], 1);
     }
     mbar_init(b.q_ready, kSoftWarps);
     mbar_init(b.dec_ready, kSoftWarps);
     mbar_init(b.o_full, 1);
     // COMPAT: one arrival per softmax warp of a 64-row criterion tile
-    for (int i = 0; i < 8; ++i) mbar_init(&b.vote[i], 2);
+    for (int i = 0; i < 8; ++i) mbar_init(b.vote[i], 2);
     *abort = 0;
     *decision = 0;
     fence_barrier_init();
@@ -282,31 +291,31 @@ struct Cta {
         const int n0 = j * BN;
         if (MODE == kQuant) {
           const int s = t % kNStg;
-          if (!mbar_wait(&b.stg_empty[s], ((t / kNStg) & 1) ^ 1, kErrTma | 2, abort)) { ok = false; break; }
+          if (!mbar_wait(b.stg_empty[s], ((t / kNStg) & 1) ^ 1, kErrTma | 2, abort)) { ok = false; break; }
           uint8_t* dst = sm + L::oStg + s * L::kStgBytes;
-          mbar_arrive_expect_tx(&b.stg_full[s], BN * (D / 2) * (lsb ? 2 : 1));
-          tma_load_4d(dst, &P.tm_k0, 0, n0, kvh, z, &b.stg_full[s]);
-          if (lsb) tma_load_4d(dst + BN * (D / 2), &P.tm_k1, 0, n0, kvh, z, &b.stg_full[s]);
+          mbar_arrive_expect_tx(b.stg_full[s], BN * (D / 2) * (lsb ? 2 : 1));
+          tma_load_4d(dst, &P.tm_k0, 0, n0, kvh, z, b.stg_full[s]);
+          if (lsb) tma_load_4d(dst + BN * (D / 2), &P.tm_k1, 0, n0, kvh, z, b.stg_full[s]);
         } else {
           const int s = t % kNExp;
-          if (!mbar_wait(&b.k_empty[s], ((t / kNExp) & 1) ^ 1, kErrTma | 3, abort)) { ok = false; break; }
+          if (!mbar_wait(b.k_empty[s], ((t / kNExp) & 1) ^ 1, kErrTma | 3, abort)) { ok = false; break; }
           uint8_t* dst = sm + L::oK + s * L::kKBytes;
-          mbar_arrive_expect_tx(&b.k_full[s], L::kKRows * D * 2);
+          mbar_arrive_expect_tx(b.k_full[s], L::kKRows * D * 2);
 #pragma unroll
           for (int a = 0; a < D / 64; ++a) {
-            tma_load_4d(dst + a * L::kKRows * 128, &P.tm_k0, 64 * a, n0, kvh, z, &b.k_full[s]);
+            tma_load_4d(dst + a * L::kKRows * 128, &P.tm_k0, 64 * a, n0, kvh, z, b.k_full[s]);
             if (MODE == kCompat)  // the tile's k_lsb rows after its k_msb rows
-              tma_load_4d(dst + a * L::kKRows * 128 + BN * 128, &P.tm_k1, 64 * a, n0, kvh, z, &b.k_full[s]);
+              tma_load_4d(dst + a * L::kKRows * 128 + BN * 128, &P.tm_k1, 64 * a, n0, kvh, z, b.k_full[s]);
           }
         }
         if (pass == 2) {
           const int s = tv % kNV;
-          if (!mbar_wait(&b.v_empty[s], ((tv / kNV) & 1) ^ 1, kErrTma | 4, abort)) { ok = false; break; }
+          if (!mbar_wait(b.v_empty[s], ((tv / kNV) & 1) ^ 1, kErrTma | 4, abort)) { ok = false; break; }
           uint8_t* dst = sm + L::oV + s * L::kVBytes;
-          mbar_arrive_expect_tx(&b.v_full[s], BN * D * 2);
+          mbar_arrive_expect_tx(b.v_full[s], BN * D * 2);
 #pragma unroll
           for (int a = 0; a < D / 64; ++a)
-            tma_load_4d(dst + a * BN * 128, &P.tm_v, 64 * a, n0, kvh, z, &b.v_full[s]);
+            tma_load_4d(dst + a * BN * 128, &P.tm_v, 64 * a, n0, kvh, z, b.v_full[s]);
           ++tv;
         }
       }
@@ -318,17 +327,17 @@ struct Cta {
   // After an abort: let the copies this thread issued land before the CTA exits.
   SPATTEN_DEV void drain_tma(uint32_t t, uint32_t tv) {
     const long long t0 = clock64();
-    auto spin = [&](uint64_t* bar, uint32_t par) {
+    auto spin = [&](SBar bar, uint32_t par) {
       while (!mbar_try_wait(bar, par) && clock64() - t0 < 200000000LL) {
       }
     };
     constexpr uint32_t ring = (MODE == kQuant) ? kNStg : kNExp;
     for (uint32_t u = (t > ring ? t - ring : 0); u < t; ++u) {
-      if (MODE == kQuant) spin(&b.stg_full[u % kNStg], (u / kNStg) & 1);
-      else spin(&b.k_full[u % kNExp], (u / kNExp) & 1);
+      if (MODE == kQuant) spin(b.stg_full[u % kNStg], (u / kNStg) & 1);
+      else spin(b.k_full[u % kNExp], (u / kNExp) & 1);
     }
     for (uint32_t u = (tv > (uint32_t)kNV ? tv - kNV : 0); u < tv; ++u)
-      spin(&b.v_full[u % kNV], (u / kNV) & 1);
+      spin(b.v_full[u % kNV], (u / kNV) & 1);
   }
 
   // ------------------------------------------------------------- expander
@@ -372,8 +381,8 @@ struct Cta {
         }
         fetch(j + 1, ks_next, kb_next);
         const int es = t % kNExp, s = t % kNStg;
-        if (MODE == kQuant && !mbar_wait(&b.stg_full[s], (t / kNStg) & 1, kErrExp | 2, abort)) return;
-        if (!mbar_wait(&b.k_empty[es], ((t / kNExp) & 1) ^ 1, kErrExp | 3, abort)) return;
+        if (MODE == kQuant && !mbar_wait(b.stg_full[s], (t / kNStg) & 1, kErrExp | 2, abort)) return;
+        if (!mbar_wait(b.k_empty[es], ((t / kNExp) & 1) ^ 1, kErrExp | 3, abort)) return;
 #pragma unroll
         for (int k = 0; k < KPT; ++k) {
           const int e = e0 + k * kExpWarps * 32;
@@ -432,8 +441,8 @@ struct Cta {
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (MODE == kQuant) mbar_arrive(&b.stg_empty[s]);
-          mbar_arrive(&b.k_full[es]);
+          if (MODE == kQuant) mbar_arrive(b.stg_empty[s]);
+          mbar_arrive(b.k_full[es]);
         }
       }
     }
@@ -469,8 +478,8 @@ struct Cta {
       for (int j = 0; j <= nt; ++j) {
         if (j < nt) {
           const int es = t % kNExp, sb = t % L::kSBuf;
-          if (!mbar_wait(&b.k_full[es], (t / kNExp) & 1, kErrMma | 3, abort)) { ok = false; break; }
-          if (!mbar_wait(&b.s_empty[sb], ((t / L::kSBuf) & 1) ^ 1, kErrMma | 4, abort)) { ok = false; break; }
+          if (!mbar_wait(b.k_full[es], (t / kNExp) & 1, kErrMma | 3, abort)) { ok = false; break; }
+          if (!mbar_wait(b.s_empty[sb], ((t / L::kSBuf) & 1) ^ 1, kErrMma | 4, abort)) { ok = false; break; }
           tc_fence_after();
           const uint32_t kaddr = smem_u32(sm + L::oK + es * L::kKBytes);
           for (int kk = 0; kk < nk; ++kk) {
@@ -480,15 +489,15 @@ struct Cta {
             if (MODE == kQuant) mma_i8(tmem + sb * L::kSW, ad, bd, idesc_s, kk > 0);
             else mma_f16(tmem + sb * L::kSW, ad, bd, idesc_s, kk > 0);
           }
-          mma_commit(&b.s_full[sb]);
-          mma_commit(&b.k_empty[es]);
+          mma_commit(b.s_full[sb]);
+          mma_commit(b.k_empty[es]);
           ++t;
         }
         if (pass == 2 && j >= 1) {  // O += P_jj V_jj, jj = j - 1
           const int jj = j - 1;
           const int pb = jj % kNP, vs = tv % kNV;
-          if (!mbar_wait(&b.p_full[pb], (jj / kNP) & 1, kErrMma | 5, abort)) { ok = false; break; }
-          if (!mbar_wait(&b.v_full[vs], (tv / kNV) & 1, kErrMma | 6, abort)) { ok = false; break; }
+          if (!mbar_wait(b.p_full[pb], (jj / kNP) & 1, kErrMma | 5, abort)) { ok = false; break; }
+          if (!mbar_wait(b.v_full[vs], (tv / kNV) & 1, kErrMma | 6, abort)) { ok = false; break; }
           tc_fence_after();
           const uint32_t paddr = smem_u32(sm + L::oP + pb * L::kPBytes);
           const uint32_t vaddr = smem_u32(sm + L::oV + vs * L::kVBytes);
@@ -499,17 +508,17 @@ struct Cta {
             mma_f16(tmem + L::kColO, ad, bd, idesc_pv, (first_pv && kk == 0) ? 0u : 1u);
           }
           first_pv = false;
-          mma_commit(&b.v_empty[vs]);
+          mma_commit(b.v_empty[vs]);
           ++tv;
           const bool pair_end = (jj & 1) || jj == nt - 1;
           if (!want_tok) {
-            mma_commit(&b.p_empty[pb]);
+            mma_commit(b.p_empty[pb]);
           } else if (pair_end) {
             // token importance of the pair's 128 keys: P'^T as an MN-major A
             // operand (the two P buffers are its two 64-key blocks, LBO apart)
             // times a [rows x 16] block of ones; K = the CTA's 128 query rows.
             const int pi = jj >> 1, cb = pi & 1;
-            if (!mbar_wait(&b.cs_empty[cb], ((pi >> 1) & 1) ^ 1, kErrMma | 7, abort)) { ok = false; break; }
+            if (!mbar_wait(b.cs_empty[cb], ((pi >> 1) & 1) ^ 1, kErrMma | 7, abort)) { ok = false; break; }
             tc_fence_after();
             const uint32_t p0 = smem_u32(sm + L::oP);
             const uint32_t ones = smem_u32(sm + L::oOnes);
@@ -519,9 +528,9 @@ struct Cta {
               const uint64_t bd = smem_desc_sw128(ones + (kk >> 2) * (kCsCols * 128) + (kk & 3) * 32, 16, 1024);
               mma_f16(tmem + L::kColCs + cb * kCsCols, ad, bd, idesc_cs, kk > 0 ? 1u : 0u);
             }
-            mma_commit(&b.cs_full[cb]);
-            if (jj & 1) mma_commit(&b.p_empty[0]);  // the pair's even tile
-            mma_commit(&b.p_empty[pb]);
+            mma_commit(b.cs_full[cb]);
+            if (jj & 1) mma_commit(b.p_empty[0]);  // the pair's even tile
+            mma_commit(b.p_empty[pb]);
           }
         }
         if (pass != 2 && j == nt - 1) break;
@@ -642,8 +651,8 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
       int* votes = reinterpret_cast<int*>(sm + L::oVote) + buf * kSoftWarps;
       if (lane == 0) votes[warp] = (wlo ? 1 : 0) | (whi ? 2 : 0);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&b.vote[buf * 4 + grp]);
-      if (!mbar_wait(&b.vote[buf * 4 + grp], (tt >> 1) & 1, kErrSoftmax | 6, abort)) {
+      if (lane == 0) mbar_arrive(b.vote[buf * 4 + grp]);
+      if (!mbar_wait(b.vote[buf * 4 + grp], (tt >> 1) & 1, kErrSoftmax | 6, abort)) {
         alive = false;
         wlo = whi = true;
       } else {
@@ -663,7 +672,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
     const int sb = t % L::kSBuf, es = t % kNExp;
     const uint32_t tt = t++;
     if (!alive) return;
-    if (!mbar_wait(&b.s_full[sb], (tt / L::kSBuf) & 1, kErrSoftmax | 1, abort)) { alive = false; return; }
+    if (!mbar_wait(b.s_full[sb], (tt / L::kSBuf) & 1, kErrSoftmax | 1, abort)) { alive = false; return; }
     tc_fence_after();
     tmem_ld32f(tl + sb * L::kSW, s);
     tmem_ld32f(tl + sb * L::kSW + 32, s + 32);
@@ -672,21 +681,25 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
     if (MODE != kCompat) {
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&b.s_empty[sb]);
+      if (lane == 0) mbar_arrive(b.s_empty[sb]);
     }
     if (MODE == kQuant && dump && valid && row % p.score_rs == 0) {
       int32_t* d = dump + (int64_t)(row / p.score_rs) * p.N + n0;
+#pragma unroll
       for (int i = 0; i < BN; ++i)
         if (n0 + i < p.N) d[i] = (int32_t)__float_as_uint(s[i]);
     }
-    if (!mbar_wait(&b.k_full[es], (tt / kNExp) & 1, kErrSoftmax | 2, abort)) { alive = false; return; }
+    if (!mbar_wait(b.k_full[es], (tt / kNExp) & 1, kErrSoftmax | 2, abort)) { alive = false; return; }
     if (MODE == kQuant) {
       // exact int32 -> fp32 (|x| < 2^22): the bits of 1.5 * 2^23 + x, minus
-      // 1.5 * 2^23; then times the key's scale
+      // 1.5 * 2^23; then times the key's scale. The key scales are read in
+      // chunks of kKsChunk columns, fenced from each other, so that the
+      // compiler does not hoist all 64 of them into registers at once.
       const float* ks = ksm + es * BN;
       const float2 nmag = make_float2(-kMagic, -kMagic);
 #pragma unroll
       for (int i = 0; i < BN; i += 4) {
+        if (kKsChunk < BN && i > 0 && i % kKsChunk == 0) asm volatile("" ::: "memory");
         const float4 k4 = *reinterpret_cast<const float4*>(ks + i);
         float2 a = __fadd2_rn(make_float2(i2f_exact(__float_as_uint(s[i])), i2f_exact(__float_as_uint(s[i + 1]))), nmag);
         float2 c = __fadd2_rn(make_float2(i2f_exact(__float_as_uint(s[i + 2])), i2f_exact(__float_as_uint(s[i + 3]))), nmag);
@@ -724,7 +737,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&b.s_empty[sb]);
+      if (lane == 0) mbar_arrive(b.s_empty[sb]);
     }
     if (prescale) {
       const float* kb = kbm + es * BN;  // key bias * log2 e (zeros without one)
@@ -741,8 +754,9 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&b.k_empty[es]);
+    if (lane == 0) mbar_arrive(b.k_empty[es]);
     if (gen_bias && valid) {
+#pragma unroll
       for (int i = 0; i < BN; ++i)
         if (n0 + i < p.N) s[i] += __ldg(brow + (int64_t)(n0 + i) * p.b_sn) * kLog2e;
     }
@@ -792,14 +806,14 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
   auto read_pair = [&](int pi) {
     const int cb = pi & 1;
     if (!alive) return;
-    if (!mbar_wait(&b.cs_full[cb], (pi >> 1) & 1, kErrSoftmax | 5, abort)) { alive = false; return; }
+    if (!mbar_wait(b.cs_full[cb], (pi >> 1) & 1, kErrSoftmax | 5, abort)) { alive = false; return; }
     tc_fence_after();
     uint32_t v;
     tmem_ld1(tl + L::kColCs + cb * kCsCols, v);
     tmem_wait_ld();
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&b.cs_empty[cb]);
+    if (lane == 0) mbar_arrive(b.cs_empty[cb]);
     const int key = pi * 2 * BN + warp * 32 + lane;
     if (key < p.N && key < nt * BN) tokp[key] = __uint_as_float(v);
   };
@@ -964,7 +978,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
         }
         // P -> shared memory: A operand of P.V (K-major) and, read as an
         // MN-major operand, of the column sums; 128B swizzle
-        if (mbar_wait(&b.p_empty[pb], ((j / kNP) & 1) ^ 1, kErrSoftmax | 3, abort)) {
+        if (mbar_wait(b.p_empty[pb], ((j / kNP) & 1) ^ 1, kErrSoftmax | 3, abort)) {
           uint8_t* prow = sm + L::oP + pb * L::kPBytes + r * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
@@ -977,7 +991,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&b.p_full[pb]);
+          if (lane == 0) mbar_arrive(b.p_full[pb]);
         } else {
           alive = false;
         }

@@ -71,6 +71,52 @@ SPATTEN_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int code,
   }
 }
 
+// The same operations on an mbarrier named by its shared-memory address: a
+// 32-bit handle that is a constant offset from the CTA's shared base, so a
+// kernel holding many barriers keeps no 64-bit pointer per barrier live.
+struct SBar {
+  uint32_t a;
+};
+struct SBarArr {  // consecutive mbarriers
+  uint32_t a;
+  SPATTEN_DEV SBar operator[](int i) const { return SBar{a + 8u * (uint32_t)i}; }
+};
+SPATTEN_DEV void mbar_init(SBar bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar.a), "r"(count));
+}
+SPATTEN_DEV void mbar_arrive(SBar bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar.a) : "memory");
+}
+SPATTEN_DEV void mbar_arrive_expect_tx(SBar bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar.a), "r"(bytes)
+               : "memory");
+}
+SPATTEN_DEV bool mbar_try_wait(SBar bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar.a), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+SPATTEN_DEV bool mbar_wait(SBar bar, uint32_t parity, unsigned int code, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      record_error(code);
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // proxies and fences
 // ---------------------------------------------------------------------------
@@ -97,6 +143,14 @@ SPATTEN_DEV void tma_load_4d(void* smem_dst, const CUtensorMap* map, int c0, int
       " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
       "r"(smem_u32(bar))
+      : "memory");
+}
+SPATTEN_DEV void tma_load_4d(void* smem_dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                             SBar bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar.a)
       : "memory");
 }
 SPATTEN_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
@@ -141,6 +195,11 @@ SPATTEN_DEV void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 // Arrive on `bar` once every tcgen05 operation issued so far by this thread completes.
+SPATTEN_DEV void mma_commit(SBar bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar.a)
+      : "memory");
+}
 SPATTEN_DEV void mma_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
