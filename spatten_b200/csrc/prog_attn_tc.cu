@@ -594,12 +594,12 @@ SPATTEN_DEV float ge_one(float a, float b) {
 }
 
 // One softmax thread per query row (TMEM lane = row) owns all 64 columns of
-// a key tile: the row statistics are thread-local. A score is carried as a
-// value s whose log2-domain score is s * cse: without a bias s is the
-// unscaled product (QUANT: the exact integer score times the key scale;
-// DENSE: q.k; COMPAT: the reference's tile-rule score) and cse the row scale
-// (q scale * sm_scale * log2 e), which the exponent's FMA applies; with a
-// bias (or a zero row scale) s is the scaled, biased score and cse = 1.
+// a key tile: the row statistics are thread-local. Scores are carried in the
+// log2 domain, s = t * cs (+ a key bias) with one rounding (t: QUANT the
+// exact integer score times the key scale, DENSE q.k, COMPAT the reference's
+// tile-rule score; cs: the row scale, q scale * sm_scale * log2 e), so that a
+// zero bias gives the same bits as none (HF materialises an all-zero mask
+// where it cannot test the user's on the host, e.g. in graph capture).
 template <int MODE, typename T, int D, bool VC>
 SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
   const int tid = threadIdx.x;      // 0 .. kSoftThreads-1
@@ -615,8 +615,6 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
   }
   const bool key_bias = p.bias != nullptr && p.b_sm == 0;
   const bool gen_bias = p.bias != nullptr && p.b_sm != 0;
-  const bool prescale = key_bias || gen_bias || !(cs > 0.f);
-  const float cse = prescale ? 1.f : cs;
   {  // ones block: B operand of the column-sum MMA (every element 1.0)
     const uint32_t one2 = pack2<T>(1.f, 1.f);
     uint4* ob = reinterpret_cast<uint4*>(sm + L::oOnes);
@@ -739,18 +737,27 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
       __syncwarp();
       if (lane == 0) mbar_arrive(b.s_empty[sb]);
     }
-    if (prescale) {
-      const float* kb = kbm + es * BN;  // key bias * log2 e (zeros without one)
+    {
       const float2 cs2 = make_float2(cs, cs);
+      if (key_bias) {  // s = t * cs + key bias * log2 e, one rounding
+        const float* kb = kbm + es * BN;
 #pragma unroll
-      for (int i = 0; i < BN; i += 4) {
-        const float4 k4 = *reinterpret_cast<const float4*>(kb + i);
-        const float2 a = __ffma2_rn(make_float2(s[i], s[i + 1]), cs2, make_float2(k4.x, k4.y));
-        const float2 c = __ffma2_rn(make_float2(s[i + 2], s[i + 3]), cs2, make_float2(k4.z, k4.w));
-        s[i] = a.x;
-        s[i + 1] = a.y;
-        s[i + 2] = c.x;
-        s[i + 3] = c.y;
+        for (int i = 0; i < BN; i += 4) {
+          const float4 k4 = *reinterpret_cast<const float4*>(kb + i);
+          const float2 a = __ffma2_rn(make_float2(s[i], s[i + 1]), cs2, make_float2(k4.x, k4.y));
+          const float2 c = __ffma2_rn(make_float2(s[i + 2], s[i + 3]), cs2, make_float2(k4.z, k4.w));
+          s[i] = a.x;
+          s[i + 1] = a.y;
+          s[i + 2] = c.x;
+          s[i + 3] = c.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < BN; i += 2) {
+          const float2 a = __fmul2_rn(make_float2(s[i], s[i + 1]), cs2);
+          s[i] = a.x;
+          s[i + 1] = a.y;
+        }
       }
     }
     __syncwarp();
@@ -781,9 +788,9 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
       a2 = fmax3(a2, s[i + 4], s[i + 5]);
       a3 = fmax3(a3, s[i + 6], s[i + 7]);
     }
-    const float mn = fmaxf(m, fmax3(fmaxf(a0, a1), a2, a3) * cse);
+    const float mn = fmaxf(m, fmax3(fmaxf(a0, a1), a2, a3));
     if (mn == -INFINITY) return;
-    const float2 c2v = make_float2(cse, cse), nm = make_float2(-mn, -mn);
+    const float2 nm = make_float2(-mn, -mn);
     float2 acc[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) acc[k] = make_float2(0.f, 0.f);
@@ -791,7 +798,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
     for (int i = 0; i < BN; i += 8) {
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const float2 x = __ffma2_rn(make_float2(s[i + 2 * k], s[i + 2 * k + 1]), c2v, nm);
+        const float2 x = __fadd2_rn(make_float2(s[i + 2 * k], s[i + 2 * k + 1]), nm);
         acc[k] = __fadd2_rn(acc[k], make_float2(fast_exp2(x.x), fast_exp2(x.y)));
       }
     }
@@ -827,7 +834,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
   int32_t* dump = (MODE == kQuant && p.score_out)
                       ? p.score_out + ((int64_t)z * p.H + h) * ((p.M + p.score_rs - 1) / p.score_rs) * (int64_t)p.N
                       : nullptr;
-  float mo = -INFINITY;  // pass 2: P = exp2(s * cse + mo)
+  float mo = -INFINITY;  // pass 2: P = exp2(s + mo)
   // Count V prune (VC): this row's kMaxVPruneCount smallest (score, key)
   // pairs of the scores it ends up using, ascending in (score, key), in
   // registers (the count-prune instantiation runs one CTA per SM with the
@@ -956,10 +963,10 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
           for (int i = 0; i < BN; ++i)
             drop |= (uint64_t)(s[i] < kvs || (s[i] == kvs && n0 + i <= kvn)) << i;
         }
-        const float2 c2v = make_float2(cse, cse), mo2 = make_float2(mo, mo);
+        const float2 mo2 = make_float2(mo, mo);
 #pragma unroll
         for (int i = 0; i < BN; i += 2) {
-          const float2 x = __ffma2_rn(make_float2(s[i], s[i + 1]), c2v, mo2);
+          const float2 x = __fadd2_rn(make_float2(s[i], s[i + 1]), mo2);
           s[i] = fast_exp2(x.x);
           s[i + 1] = fast_exp2(x.y);
         }
