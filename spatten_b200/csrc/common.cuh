@@ -118,11 +118,35 @@ SPATTEN_DEV float fast_exp2(float x) {
 // rint(__fdiv_rn(x, sc)) gives, for |x| <= 127 * sc: x * (1 / sc) is within
 // 2 ulp of x / sc, so its rounding can only differ when it lies within a few
 // ulp of a half-integer; those rare values take the exact division.
+// y rounded to the nearest integer, ties to even, for |y| < 2^22 (other
+// inputs give garbage, which the callers' tie test sends to the exact path):
+// y + 1.5 * 2^23 lands in [2^23, 2^24), where the spacing of floats is 1,
+// so the round-to-nearest addition leaves rint(y) in the low mantissa bits.
+// FMA-pipe adds instead of the conversion pipe's round + float-to-int.
+SPATTEN_DEV int rint_small(float y, float& ti) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  const float f = __fadd_rn(y, kRound);
+  ti = __fsub_rn(f, kRound);
+  return __float_as_int(f) - 0x4B400000;
+}
+
 SPATTEN_DEV int quant_div(float x, float sc, float rc) {
   const float y = x * rc;
   const float t = rintf(y);
   if (!(fabsf(y - t) <= 0.49990f)) return __float2int_rn(__fdiv_rn(x, sc));  // also NaN / inf (denormal sc)
   return (int)t;
+}
+
+// The same result with the rounding on the FMA pipe (rint_small), for
+// kernels that quantise every value through this call; it holds a few more
+// registers, so the kernels that call quant_div only on the rare near-tie
+// path keep the version above.
+SPATTEN_DEV int quant_div_fadd(float x, float sc, float rc) {
+  const float y = x * rc;
+  float t;
+  const int n = rint_small(y, t);
+  if (!(fabsf(y - t) <= 0.49990f)) return __float2int_rn(__fdiv_rn(x, sc));  // also NaN / inf (denormal sc)
+  return n;
 }
 
 // a / 127 rounded to nearest even (the quantisation scale max|x| / 127), for

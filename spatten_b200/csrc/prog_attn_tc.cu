@@ -344,7 +344,6 @@ struct Cta {
   SPATTEN_DEV void expand_role() {
     constexpr int KPT = BN / (kExpWarps * 32);  // keys of a tile per expander thread
     const int e0 = threadIdx.x - kWarpExp * 32;  // this thread's first key within the tile
-    const int lane = threadIdx.x & 31;
     const float* ksrc = (MODE == kQuant) ? p.k_scale + ((int64_t)z * p.Hkv + kvh) * p.N : nullptr;
     const bool key_bias = p.bias != nullptr && p.b_sm == 0;
     const float* bsrc = key_bias ? p.bias + (int64_t)z * p.b_sz + (int64_t)h * p.b_sh : nullptr;
@@ -440,10 +439,8 @@ struct Cta {
         // per SM) -- and the K' rows written here are read by the MMA.
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          if (MODE == kQuant) mbar_arrive(b.stg_empty[s]);
-          mbar_arrive(b.k_full[es]);
-        }
+        if (MODE == kQuant) mbar_arrive_elect(b.stg_empty[s]);
+        mbar_arrive_elect(b.k_full[es]);
       }
     }
   }
@@ -623,7 +620,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
   load_q_row(r, valid);
   fence_proxy_async_smem();
   __syncwarp();
-  if (lane == 0) mbar_arrive(b.q_ready);
+  mbar_arrive_elect(b.q_ready);
 
   const float* brow = gen_bias ? p.bias + (int64_t)z * p.b_sz + (int64_t)h * p.b_sh + (int64_t)row * p.b_sm
                                : nullptr;
@@ -679,7 +676,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
     if (MODE != kCompat) {
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(b.s_empty[sb]);
+      mbar_arrive_elect(b.s_empty[sb]);
     }
     if (MODE == kQuant && dump && valid && row % p.score_rs == 0) {
       int32_t* d = dump + (int64_t)(row / p.score_rs) * p.N + n0;
@@ -735,7 +732,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(b.s_empty[sb]);
+      mbar_arrive_elect(b.s_empty[sb]);
     }
     {
       const float2 cs2 = make_float2(cs, cs);
@@ -761,7 +758,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(b.k_empty[es]);
+    mbar_arrive_elect(b.k_empty[es]);
     if (gen_bias && valid) {
 #pragma unroll
       for (int i = 0; i < BN; ++i)
@@ -820,7 +817,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
     tmem_wait_ld();
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(b.cs_empty[cb]);
+    mbar_arrive_elect(b.cs_empty[cb]);
     const int key = pi * 2 * BN + warp * 32 + lane;
     if (key < p.N && key < nt * BN) tokp[key] = __uint_as_float(v);
   };
@@ -915,7 +912,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
         if (p.refetch_out && valid) p.refetch_out[((int64_t)z * p.H + h) * p.M + row] = flag;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(b.dec_ready);
+      mbar_arrive_elect(b.dec_ready);
       if (!(MODE == kQuant && any)) continue;
       warp_any = __any_sync(0xffffffffu, flag);
     }
@@ -998,7 +995,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(b.p_full[pb]);
+          mbar_arrive_elect(b.p_full[pb]);
         } else {
           alive = false;
         }

@@ -31,9 +31,16 @@ namespace spatten {
 
 namespace {
 
+// a and b rounded to T (nearest even) by one packed conversion, which halves
+// the conversion-pipe work of rounding every intermediate to T; returns the
+// packed pair
 template <typename T>
-SPATTEN_DEV float rnd(float x) {
-  return to_f32<T>(from_f32<T>(x));
+SPATTEN_DEV uint32_t rnd2(float& a, float& b) {
+  const uint32_t u = pack2<T>(a, b);
+  const T* e = reinterpret_cast<const T*>(&u);
+  a = to_f32<T>(e[0]);
+  b = to_f32<T>(e[1]);
+  return u;
 }
 
 template <typename T>
@@ -42,16 +49,6 @@ SPATTEN_DEV void load8(const T* p, float (&f)[8]) {
   const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
   for (int i = 0; i < 8; ++i) f[i] = to_f32<T>(e[i]);
-}
-
-template <typename T>
-SPATTEN_DEV void store8(T* p, const float (&f)[8]) {
-  uint4 u;
-  u.x = pack2<T>(f[0], f[1]);
-  u.y = pack2<T>(f[2], f[3]);
-  u.z = pack2<T>(f[4], f[5]);
-  u.w = pack2<T>(f[6], f[7]);
-  *reinterpret_cast<uint4*>(p) = u;
 }
 
 template <typename T, int D>
@@ -92,23 +89,37 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(const QkPrepParams p) {
     const float inv = rsqrtf(ss * (1.0f / (float)D) + p.eps);
     float n[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) n[i] = rnd<T>((isq ? wq[i] : wk[i]) * rnd<T>(x[i] * inv));
+    for (int i = 0; i < 8; i += 2) {
+      float a = x[i] * inv, b = x[i + 1] * inv;
+      rnd2<T>(a, b);
+      n[i] = (isq ? wq[i] : wk[i]) * a;
+      n[i + 1] = (isq ? wq[i + 1] : wk[i + 1]) * b;
+      rnd2<T>(n[i], n[i + 1]);
+    }
     // rotary partner: dims d +- D/2 live LPR/2 lanes away
     float pn[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) pn[i] = __shfl_xor_sync(0xffffffffu, n[i], LPR / 2);
     const bool first_half = li < LPR / 2;
     float o[8];
+    uint4 packed;  // o as T, for the stores
+    uint32_t* pw = reinterpret_cast<uint32_t*>(&packed);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float rot = first_half ? -pn[i] : pn[i];
-      o[i] = rnd<T>(rnd<T>(n[i] * c[i]) + rnd<T>(rot * sn[i]));
+    for (int i = 0; i < 8; i += 2) {
+      float a0 = n[i] * c[i], a1 = n[i + 1] * c[i + 1];
+      float b0 = (first_half ? -pn[i] : pn[i]) * sn[i], b1 = (first_half ? -pn[i + 1] : pn[i + 1]) * sn[i + 1];
+      rnd2<T>(a0, a1);
+      rnd2<T>(b0, b1);
+      o[i] = a0 + b0;
+      o[i + 1] = a1 + b1;
+      pw[i >> 1] = rnd2<T>(o[i], o[i + 1]);
     }
     if (!isq) {
-      if (live) store8<T>(static_cast<T*>(p.k_out) + tok * p.ko_st + (int64_t)h * D + li * 8, o);
+      if (live) *reinterpret_cast<uint4*>(static_cast<T*>(p.k_out) + tok * p.ko_st + (int64_t)h * D + li * 8) = packed;
       continue;
     }
-    if (p.q_out && live) store8<T>(static_cast<T*>(p.q_out) + tok * p.qo_st + (int64_t)h * D + li * 8, o);
+    if (p.q_out && live)
+      *reinterpret_cast<uint4*>(static_cast<T*>(p.q_out) + tok * p.qo_st + (int64_t)h * D + li * 8) = packed;
     if (p.q8) {
       float amax = 0.f;
 #pragma unroll
@@ -120,7 +131,7 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(const QkPrepParams p) {
       uint32_t w[2] = {0u, 0u};
       if (sc != 0.f) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) w[i >> 2] |= ((uint32_t)quant_div(o[i], sc, rc) & 0xFFu) << (8 * (i & 3));
+        for (int i = 0; i < 8; ++i) w[i >> 2] |= ((uint32_t)quant_div_fadd(o[i], sc, rc) & 0xFFu) << (8 * (i & 3));
       }
       if (live) {
         const int64_t orow = ((int64_t)b * p.Hq + h) * p.S + s;

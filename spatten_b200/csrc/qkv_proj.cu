@@ -158,9 +158,10 @@ SPATTEN_DEV void epilogue_head(const ProjParams& p, uint32_t tl, const Tile& tl_
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       x[e] = round_to<T>(__uint_as_float(a[i + e]) + sb[c + e]);
-      const float y = x[e] * rc, ti = rintf(y);
+      const float y = x[e] * rc;
+      float ti;
+      t[e] = rint_small(y, ti);
       near_tie |= !(fabsf(y - ti) <= 0.49990f);
-      t[e] = (int)ti;
     }
     if (near_tie) {
 #pragma unroll

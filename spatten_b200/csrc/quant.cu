@@ -164,9 +164,10 @@ __global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict
     bool near_tie = false;
 #pragma unroll
     for (int i = 0; i < EPL; ++i) {
-      const float y = v[i] * rs, ti = rintf(y);
+      const float y = v[i] * rs;
+      float ti;
+      t[i] = rint_small(y, ti);
       near_tie |= !(fabsf(y - ti) <= 0.49990f);
-      t[i] = (int)ti;
     }
     if (s == 0.f) {
 #pragma unroll
@@ -217,9 +218,22 @@ __global__ void __launch_bounds__(256) quant_rows_vec_kernel(const T* __restrict
 template <typename T, int D, bool PLANES>
 static cudaError_t launch_quant_vec(const T* x, int Z, int H, int M, int64_t sz, int64_t sh, int64_t sm,
                                     int8_t* q8, uint8_t* msb, uint8_t* lsb, float* scale, cudaStream_t st,
-                                    int64_t blocks) {
+                                    int64_t blocks, int n_sm) {
   constexpr int LPR = D / (32 / (int)sizeof(T));
   if constexpr (LPR >= 2 && LPR <= 32) {
+    // one wave: the grid-stride loop gives every resident block the same
+    // share of rows (more blocks than fit would leave a partial last wave)
+    static int per_sm = 0;
+    if (per_sm == 0) {
+      int n = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, quant_rows_vec_kernel<T, D, PLANES>, 256, 0) !=
+              cudaSuccess ||
+          n < 1)
+        n = 1;
+      per_sm = n;
+    }
+    const int64_t wave = (int64_t)per_sm * (n_sm > 0 ? n_sm : 1);
+    if (blocks > wave) blocks = wave;
     quant_rows_vec_kernel<T, D, PLANES><<<(unsigned)blocks, 256, 0, st>>>(x, Z, H, M, sz, sh, sm, q8, msb,
                                                                           lsb, scale);
     return cudaGetLastError();
@@ -248,10 +262,10 @@ static cudaError_t launch_quant_t(const void* x, int Z, int H, int M, int D, int
     if (vblocks > cap) vblocks = cap;
     if (vblocks < 1) vblocks = 1;
     switch (D) {
-      case 32: return launch_quant_vec<T, 32, PLANES>(xp, Z, H, M, sz, sh, sm, q8, msb, lsb, scale, st, vblocks);
-      case 64: return launch_quant_vec<T, 64, PLANES>(xp, Z, H, M, sz, sh, sm, q8, msb, lsb, scale, st, vblocks);
-      case 128: return launch_quant_vec<T, 128, PLANES>(xp, Z, H, M, sz, sh, sm, q8, msb, lsb, scale, st, vblocks);
-      case 256: return launch_quant_vec<T, 256, PLANES>(xp, Z, H, M, sz, sh, sm, q8, msb, lsb, scale, st, vblocks);
+      case 32: return launch_quant_vec<T, 32, PLANES>(xp, Z, H, M, sz, sh, sm, q8, msb, lsb, scale, st, vblocks, n_sm);
+      case 64: return launch_quant_vec<T, 64, PLANES>(xp, Z, H, M, sz, sh, sm, q8, msb, lsb, scale, st, vblocks, n_sm);
+      case 128: return launch_quant_vec<T, 128, PLANES>(xp, Z, H, M, sz, sh, sm, q8, msb, lsb, scale, st, vblocks, n_sm);
+      case 256: return launch_quant_vec<T, 256, PLANES>(xp, Z, H, M, sz, sh, sm, q8, msb, lsb, scale, st, vblocks, n_sm);
       default: return cudaErrorInvalidValue;
     }
   }

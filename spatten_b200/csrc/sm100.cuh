@@ -91,6 +91,14 @@ SPATTEN_DEV void mbar_arrive_expect_tx(SBar bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar.a), "r"(bytes)
                : "memory");
 }
+// One lane of a converged warp (elect.sync) arrives; predicated, so the warp
+// takes no divergent branch.
+SPATTEN_DEV void mbar_arrive_elect(SBar bar) {
+  asm volatile(
+      "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n"
+      " @p mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];\n}\n" ::"r"(bar.a)
+      : "memory");
+}
 SPATTEN_DEV bool mbar_try_wait(SBar bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

@@ -189,7 +189,8 @@ def prog_attn(q, k0, v, *, mode, k1=None, q_scale=None, k_scale=None, sm_scale=N
     ws_bytes = N.lib.spatten_prog_attn_workspace_size(a)
     ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=v.device)
     N.check(N.lib.spatten_prog_attn(a, ws.data_ptr() if ws_bytes else None, ws_bytes, _stream(v)))
-    return AttnResult(out, tok, head, None if ref is None else ref.bool(), sco)
+    # the kernel writes 0 / 1 bytes: a bool view, no conversion launch
+    return AttnResult(out, tok, head, None if ref is None else ref.view(torch.bool), sco)
 
 
 def _float_planes(*ts):
