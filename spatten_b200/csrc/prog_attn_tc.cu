@@ -69,6 +69,15 @@ constexpr int kNV = 2;         // V stages
 constexpr int kNP = 2;         // P buffers
 constexpr int kCsCols = 16;    // N of the column-sum MMA (16 identical columns)
 constexpr int kWarpTma = kSoftWarps, kWarpMma = kSoftWarps + 1, kWarpExp = kSoftWarps + 2;
+// The two-CTA-per-SM instantiations (D = 64, no count prune) move registers
+// from the producer warpgroup to the softmax warpgroup (setmaxnreg); the
+// split adds up to the CTA's allocation only at kSplitLaunchRegs registers a
+// thread, which the launcher checks before every first launch.
+template <int D, bool VC>
+constexpr bool kRegSplit = (D == 64 && !VC);
+constexpr int kSplitLaunchRegs = 128;
+static_assert(kSoftThreads * 160 + (kThreads - kSoftThreads) * 96 == kThreads * kSplitLaunchRegs,
+              "register split must add up to the launch allocation");
 
 enum Mode : int { kQuant = 0, kDense = 1, kCompat = 2 };
 
@@ -671,6 +680,8 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
     tc_fence_after();
     tmem_ld32f(tl + sb * L::kSW, s);
     tmem_ld32f(tl + sb * L::kSW + 32, s + 32);
+    // the key scales / bias of this tile: waited for while the load is in flight
+    const bool k_ok = mbar_wait(b.k_full[es], (tt / kNExp) & 1, kErrSoftmax | 2, abort);
     tmem_wait_ld();
     const int n0 = j * BN;
     if (MODE != kCompat) {
@@ -684,7 +695,7 @@ SPATTEN_DEV void Cta<MODE, T, D, VC>::softmax_role() {
       for (int i = 0; i < BN; ++i)
         if (n0 + i < p.N) d[i] = (int32_t)__float_as_uint(s[i]);
     }
-    if (!mbar_wait(b.k_full[es], (tt / kNExp) & 1, kErrSoftmax | 2, abort)) { alive = false; return; }
+    if (!k_ok) { alive = false; return; }
     if (MODE == kQuant) {
       // exact int32 -> fp32 (|x| < 2^22): the bits of 1.5 * 2^23 + x, minus
       // 1.5 * 2^23; then times the key's scale. The key scales are read in
@@ -1078,10 +1089,19 @@ __global__ void __launch_bounds__(kThreads, (D == 64 && !VC) ? 2 : 1)
   tc_fence_after();
   c.tmem = *tslot;
   c.nt = *reinterpret_cast<volatile int*>(base + L::oFlag + 8);
-  if (warp < kSoftWarps) c.softmax_role();
-  else if (warp == kWarpTma) c.tma_role();
-  else if (warp == kWarpMma) c.mma_role();
-  else c.expand_role();
+  // Two CTAs per SM launch at kSplitLaunchRegs registers a thread (the host
+  // refuses the launch otherwise); the softmax warpgroup takes 160 of them
+  // and the producer warpgroup (TMA, MMA, expanders) keeps 96:
+  // 128 * 160 + 128 * 96 = 256 * 128, the CTA's launch allocation.
+  if (warp < kSoftWarps) {
+    if (kRegSplit<D, VC>) asm volatile("setmaxnreg.inc.sync.aligned.u32 160;\n" ::: "memory");
+    c.softmax_role();
+  } else {
+    if (kRegSplit<D, VC>) asm volatile("setmaxnreg.dec.sync.aligned.u32 96;\n" ::: "memory");
+    if (warp == kWarpTma) c.tma_role();
+    else if (warp == kWarpMma) c.mma_role();
+    else c.expand_role();
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == kWarpMma) {
@@ -1153,6 +1173,18 @@ cudaError_t launch_tc_t(const AttnParams& a, cudaStream_t st) {
   auto kern = prog_attn_tc_kernel<MODE, T, D, VC>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   if (e != cudaSuccess) return e;
+  if (kRegSplit<D, VC>) {
+    // the register split adds up only at this launch allocation; with any
+    // other, setmaxnreg.inc would wait for registers the CTA does not hold
+    static int regs = -1;  // one per instantiation
+    if (regs < 0) {
+      cudaFuncAttributes fa;
+      e = cudaFuncGetAttributes(&fa, kern);
+      if (e != cudaSuccess) return e;
+      regs = fa.numRegs;
+    }
+    if (regs != kSplitLaunchRegs) return cudaErrorInvalidConfiguration;
+  }
   dim3 grid((unsigned)a.mtiles, (unsigned)a.H, (unsigned)a.Z);
   kern<<<grid, kThreads, L::kAlloc, st>>>(P);
   return cudaGetLastError();
