@@ -38,6 +38,9 @@
  *       the next layer's hidden-state gather (module.py:49-54) moved into the
  *       attention output projection + residual, so the FFN runs on the
  *       compacted sequence.
+ *   spatten_add_layer_norm
+ *       the residual add + LayerNorm of the HF BertLayer tail that the
+ *       reference's encoder loop runs per layer (module.py:75).
  */
 #ifndef SPATTEN_B200_H
 #define SPATTEN_B200_H
@@ -372,6 +375,21 @@ int spatten_gather_rows(const void* src, int64_t src_b_stride, int64_t src_r_str
                         int rows_per_idx,
                         int64_t idx_scale, int64_t row_bytes, void* dst, int64_t dst_b_stride,
                         int64_t dst_r_stride, void* stream);
+
+/*
+ * Residual add + LayerNorm over rows of n features (f16 / bf16):
+ *   h = x + res (rounded to the element type; res may be NULL),
+ *   y = (h - mean(h)) / sqrt(var(h) + eps) * gamma + beta
+ * with the mean and the biased variance in fp32. Replaces, in the tail of
+ * the HF BertLayer that the reference's encoder loop runs for every layer
+ * (module.py:75), torch's add + layer_norm of BertOutput and the layer_norm
+ * of BertSelfOutput (after spatten_compact_out_proj). Row strides in
+ * elements; every row, gamma and beta start on a 16-byte boundary; n one of
+ * 256, 512, 768, 1024, 1536, 2048 (SPATTEN_ERR_UNSUPPORTED otherwise).
+ */
+int spatten_add_layer_norm(const void* x, int64_t x_row_stride, const void* res, int64_t res_row_stride,
+                           const void* gamma, const void* beta, void* y, int64_t y_row_stride,
+                           int64_t rows, int n, int dtype, float eps, void* stream);
 
 #ifdef __cplusplus
 }

@@ -113,6 +113,8 @@ SIGNATURES = {
     "spatten_compact_out_proj": (c_int, [ctypes.POINTER(CompactOutProjArgs), c_vp]),
     "spatten_gather_rows": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_int, c_int, c_int,
                                     c_i64, c_i64, c_vp, c_i64, c_i64, c_vp]),
+    "spatten_add_layer_norm": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_int,
+                                       c_int, ctypes.c_float, c_vp]),
 }
 
 

@@ -48,7 +48,7 @@ from transformers.pytorch_utils import apply_chunking_to_forward
 
 from . import _native as N
 from .progressive import prog_attn, quant_k_planes, quant_q_int8
-from .proj import compact_out_proj, qkv_proj
+from .proj import LAYER_NORM_FEATURES, add_layer_norm, compact_out_proj, qkv_proj
 from .select import gather_head_rows, gather_rows, topk_indices
 
 
@@ -185,7 +185,10 @@ class SpattenBertSelfAttention(BertSelfAttention):
                     raise NotImplementedError(
                         f"v_prune_num={v_count}: the B200 path prunes at most "
                         f"{N.MAX_V_PRUNE_COUNT} keys per row by count; use v_prune_threshold")
-        full = torch.zeros(B, S, H, d, dtype=hidden_states.dtype, device=dev)
+        # the context of the pruned heads reads as zeros (every head slot is
+        # written when all heads are active)
+        alloc = torch.empty if cur == H else torch.zeros
+        full = alloc(B, S, H, d, dtype=hidden_states.dtype, device=dev)
         cum = self.cumulative_token_score
         common = dict(sm_scale=1.0 / math.sqrt(d), v_thr=v_thr, v_prune_count=v_count, bias=bias,
                       tok_in=cum,
@@ -244,20 +247,38 @@ def _compactable(layer, attn, hidden_states, last):
             and hidden_states.shape[-1] % 32 == 0)
 
 
+def _ln_fusable(ln, x):
+    """Whether ``ln`` (an nn.LayerNorm over x's last dimension) can run as
+    spatten_add_layer_norm."""
+    return (isinstance(ln, torch.nn.LayerNorm) and ln.elementwise_affine and ln.weight is not None
+            and ln.bias is not None and tuple(ln.normalized_shape) == (x.shape[-1],)
+            and x.shape[-1] in LAYER_NORM_FEATURES and ln.weight.dtype == x.dtype
+            and ln.bias.dtype == x.dtype)
+
+
 def _layer_tail(layer, attn, ctx, hidden_states, kept):
     """HF BertLayer after its self-attention (BertSelfOutput, then the FFN
     chunk). With ``kept`` the next layer's token gather (module.py:49-54)
     runs first, folded into the output projection's row loads
     (``compact_out_proj``): every step of the tail is row-wise, so its rows
     for the kept tokens are the reference's rows, and the FFN skips the rows
-    the next layer drops."""
+    the next layer drops. The LayerNorms (and BertOutput's residual add) run
+    as spatten_add_layer_norm; the FFN's dense layers and GELU stay HF's
+    modules."""
     so = layer.attention.output
     if kept is None:
         a = so(ctx, hidden_states)
     else:
         y = compact_out_proj(ctx, hidden_states, kept, so.dense.weight, so.dense.bias,
                              attn.num_heads, attn.head_dim, heads=attn.active_head_indices_for_this_layer)
-        a = so.LayerNorm(y)
+        ln = so.LayerNorm
+        a = add_layer_norm(y, ln.weight, ln.bias, ln.eps) if _ln_fusable(ln, y) else ln(y)
+    out = layer.output
+    if (layer.chunk_size_feed_forward == 0 and hasattr(layer, "intermediate") and hasattr(out, "dense")
+            and not out.training and _ln_fusable(getattr(out, "LayerNorm", None), a)):
+        # BertOutput: LayerNorm(dense(intermediate) + a), dropout off in eval
+        h = out.dense(layer.intermediate(a))
+        return add_layer_norm(h, out.LayerNorm.weight, out.LayerNorm.bias, out.LayerNorm.eps, residual=a)
     return apply_chunking_to_forward(layer.feed_forward_chunk, layer.chunk_size_feed_forward,
                                      layer.seq_len_dim, a)
 
@@ -276,6 +297,14 @@ def spatten_encoder_forward(self, hidden_states, attention_mask=None, **kwargs):
     cumulative = None
     compacted = False
     n_layers = len(self.layer)
+    if attention_mask is not None:
+        # the key mask as an additive fp32 bias [B, 1, 1, S], converted once:
+        # the layers gather its kept columns and read it as it is
+        B0 = hidden_states.shape[0]
+        attention_mask = _mask_bias(attention_mask, B0, hidden_states.shape[1]).expand(B0, -1, -1, -1)
+        if attention_mask.shape[2] > 1:
+            attention_mask = attention_mask[:, :, :1, :]
+        attention_mask = attention_mask.contiguous()
     for i, layer in enumerate(self.layer):
         if active_tokens is not None:
             if not compacted:

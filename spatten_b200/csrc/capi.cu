@@ -263,6 +263,33 @@ int spatten_gather_rows(const void* src, int64_t src_b_stride, int64_t src_r_str
                      "gather launch");
 }
 
+int spatten_add_layer_norm(const void* x, int64_t x_row_stride, const void* res, int64_t res_row_stride,
+                           const void* gamma, const void* beta, void* y, int64_t y_row_stride,
+                           int64_t rows, int n, int dtype, float eps, void* stream) {
+  if (rows < 0 || n < 1) return fail(SPATTEN_ERR_INVALID, "add_layer_norm: bad sizes rows=%lld n=%d",
+                                     (long long)rows, n);
+  if (rows == 0) return ok();  // nothing to read or write (empty tensors may have null data)
+  if (!x || !gamma || !beta || !y) return fail(SPATTEN_ERR_INVALID, "add_layer_norm: null pointer");
+  if (dtype != SPATTEN_DTYPE_F16 && dtype != SPATTEN_DTYPE_BF16)
+    return fail(SPATTEN_ERR_UNSUPPORTED, "add_layer_norm: dtype %d (need f16 or bf16)", dtype);
+  if (!spatten::add_layer_norm_supported(n))
+    return fail(SPATTEN_ERR_UNSUPPORTED, "add_layer_norm: n=%d (need 256, 512, 768, 1024, 1536 or 2048)", n);
+  if (!(eps >= 0.f)) return fail(SPATTEN_ERR_INVALID, "add_layer_norm: eps must be >= 0");
+  if (x_row_stride < n || y_row_stride < n || (res && res_row_stride < n))
+    return fail(SPATTEN_ERR_INVALID, "add_layer_norm: row stride below n");
+  // 16-byte rows: every row start (base + r * stride * 2 bytes) on a 16-byte boundary
+  auto a16 = [](const void* p, int64_t s) {
+    return (reinterpret_cast<uintptr_t>(p) % 16) == 0 && (s * 2) % 16 == 0;
+  };
+  if (!a16(x, x_row_stride) || !a16(y, y_row_stride) || (res && !a16(res, res_row_stride)) ||
+      !a16(gamma, 0) || !a16(beta, 0))
+    return fail(SPATTEN_ERR_INVALID, "add_layer_norm: rows, gamma and beta must start on 16-byte boundaries");
+  return cuda_status(spatten::launch_add_layer_norm(x, res, gamma, beta, y, rows, n, x_row_stride,
+                                                    res_row_stride, y_row_stride, dtype, eps,
+                                                    (cudaStream_t)stream),
+                     "add_layer_norm launch");
+}
+
 // mode 0: sizing (shape and input checks only), 1: importance, 2: attend
 static int fill_decode(const spatten_decode_args* a, spatten::DecodeParams& p, int mode) {
   const bool attend = mode == 2;

@@ -74,6 +74,12 @@ cudaError_t launch_gather(const void* src, int64_t src_b, int64_t src_r, const i
                           int64_t row_bytes, void* dst, int64_t dst_b, int64_t dst_r,
                           cudaStream_t st, int n_sm, int64_t src_rows);
 
+// Residual add + LayerNorm over rows of n features (layernorm.cu).
+bool add_layer_norm_supported(int n);
+cudaError_t launch_add_layer_norm(const void* x, const void* res, const void* gamma, const void* beta,
+                                  void* y, int64_t rows, int n, int64_t xs, int64_t rs, int64_t ys,
+                                  int dtype, float eps, cudaStream_t st);
+
 // Per-head RMSNorm + rotary embedding of Q and K, Q quantised (qk_prep.cu).
 struct QkPrepParams {
   int dtype;                 // kF16 / kBF16: projections, weights, cos / sin, outputs

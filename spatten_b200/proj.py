@@ -146,3 +146,40 @@ def compact_out_proj(ctx, res, kept, w, bias, num_heads, head_dim, heads=None):
     a.out = out.data_ptr()
     N.check(N.lib.spatten_compact_out_proj(a, _stream(ctx)))
     return out
+
+
+LAYER_NORM_FEATURES = (256, 512, 768, 1024, 1536, 2048)
+
+
+def add_layer_norm(x, weight, bias, eps, residual=None):
+    """LayerNorm of ``x`` (+ ``residual``, the sum rounded to x's dtype as
+    torch's add rounds it) over the last dimension, with affine ``weight`` /
+    ``bias`` (host side of spatten_add_layer_norm): the residual add +
+    LayerNorm of HF's BertOutput and the LayerNorm of BertSelfOutput in one
+    launch. fp16 / bf16, last dimension in ``LAYER_NORM_FEATURES``; x,
+    residual, weight and bias share one dtype. Returns a new tensor shaped
+    like x."""
+    if not (x.is_cuda and weight.is_cuda and bias.is_cuda):
+        raise ValueError("add_layer_norm takes CUDA tensors; there is no CPU path")
+    if x.dtype not in (torch.float16, torch.bfloat16) or weight.dtype != x.dtype or bias.dtype != x.dtype:
+        raise ValueError("add_layer_norm: x, weight and bias must share one dtype, fp16 or bf16")
+    n = x.shape[-1]
+    if weight.numel() != n or bias.numel() != n:
+        raise ValueError(f"add_layer_norm: weight / bias of {weight.numel()} / {bias.numel()} for {n} features")
+    x2 = x.reshape(-1, n)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    r2 = None
+    if residual is not None:
+        if residual.shape != x.shape or residual.dtype != x.dtype:
+            raise ValueError("add_layer_norm: residual must match x's shape and dtype")
+        r2 = residual.reshape(-1, n)
+        if r2.stride(-1) != 1:
+            r2 = r2.contiguous()
+    y = torch.empty(x2.shape, dtype=x.dtype, device=x.device)
+    w, b = weight.contiguous(), bias.contiguous()
+    N.check(N.lib.spatten_add_layer_norm(
+        x2.data_ptr(), x2.stride(0), None if r2 is None else r2.data_ptr(), 0 if r2 is None else r2.stride(0),
+        w.data_ptr(), b.data_ptr(), y.data_ptr(), y.stride(0), x2.shape[0], n, _DT[x.dtype], float(eps),
+        _stream(x)))
+    return y.view(x.shape)

@@ -248,3 +248,22 @@ def test_compat_rejects_masks():
         a = _args(N, mode=N.MODE_COMPAT, tile_m=32, tile_n=32)
         setattr(a, field, val)
         assert N.lib.spatten_prog_attn(a, None, 0, None) == N.ERR_UNSUPPORTED, field
+
+
+def test_add_layer_norm_args_validation():
+    """The residual add + LayerNorm rejects bad arguments before any launch;
+    zero rows is a no-op (empty tensors may carry null pointers)."""
+    from spatten_b200 import _native as N
+    f = N.lib.spatten_add_layer_norm
+    p = 1 << 20
+    # x, x_stride, res, res_stride, gamma, beta, y, y_stride, rows, n, dtype, eps, stream
+    assert f(None, 768, None, 0, p, p, p, 768, 10, 768, N.DTYPE_F16, 1e-12, None) == N.ERR_INVALID
+    assert f(p, 768, None, 0, p, p, p, 768, 10, 768, N.DTYPE_F32, 1e-12, None) == N.ERR_UNSUPPORTED
+    assert f(p, 768, None, 0, p, p, p, 768, 10, 700, N.DTYPE_F16, 1e-12, None) == N.ERR_UNSUPPORTED
+    assert f(p, 700, None, 0, p, p, p, 768, 10, 768, N.DTYPE_F16, 1e-12, None) == N.ERR_INVALID  # stride < n
+    assert f(p, 768, p, 100, p, p, p, 768, 10, 768, N.DTYPE_F16, 1e-12, None) == N.ERR_INVALID  # res stride
+    assert f(p + 8, 768, None, 0, p, p, p, 768, 10, 768, N.DTYPE_BF16, 1e-12, None) == N.ERR_INVALID  # align
+    assert f(p, 772, None, 0, p, p, p, 768, 10, 768, N.DTYPE_BF16, 1e-12, None) == N.ERR_INVALID  # row align
+    assert f(p, 768, None, 0, p, p, p, 768, 10, 768, N.DTYPE_F16, -1.0, None) == N.ERR_INVALID  # eps
+    assert f(p, 768, None, 0, p, p, p, 768, -1, 768, N.DTYPE_F16, 1e-12, None) == N.ERR_INVALID
+    assert f(None, 0, None, 0, None, None, None, 0, 0, 768, N.DTYPE_F16, 1e-12, None) == N.OK

@@ -153,3 +153,50 @@ def test_compact_out_proj_matches_torch(case):
     got = out.cpu()
     torch.testing.assert_close(got.float(), ref.float(), rtol=2 * RTOL[dt], atol=OUT_ATOL[dt])
     assert (got == ref).float().mean().item() > 0.97
+
+
+LN_CASES = [
+    # rows, n, dtype, residual, eps
+    (32 * 461, 768, torch.float16, True, 1e-12),
+    (1000, 768, torch.float16, False, 1e-12),
+    (77, 1024, torch.bfloat16, True, 1e-5),
+    (9, 256, torch.bfloat16, False, 1e-6),
+    (1, 2048, torch.float16, True, 1e-5),
+    (0, 768, torch.float16, True, 1e-12),
+]
+
+
+@pytest.mark.parametrize("case", LN_CASES)
+def test_add_layer_norm_matches_torch(case):
+    """spatten_add_layer_norm against torch's add (rounded to the dtype) +
+    F.layer_norm on the same GPU tensors: the statistics are summed in a
+    different order (two passes in registers against Welford), so an output
+    may differ by one ulp; > 98 % identical."""
+    from spatten_b200.proj import add_layer_norm
+    rows, n, dt, with_res, eps = case
+    g = torch.Generator().manual_seed(rows + n)
+    x = (torch.randn(rows, n, generator=g) * 3 + 0.5).to(dt).cuda()
+    res = torch.randn(rows, n, generator=g).to(dt).cuda() if with_res else None
+    w = (1 + 0.1 * torch.randn(n, generator=g)).to(dt).cuda()
+    b = (0.1 * torch.randn(n, generator=g)).to(dt).cuda()
+    got = add_layer_norm(x, w, b, eps, residual=res)
+    h = x + res if with_res else x
+    ref = torch.nn.functional.layer_norm(h, (n,), w, b, eps)
+    assert got.shape == x.shape and got.dtype == dt
+    if rows == 0:
+        return
+    torch.testing.assert_close(got.float(), ref.float(), rtol=RTOL[dt], atol=RTOL[dt])
+    assert (got == ref).float().mean().item() > 0.98
+
+
+def test_add_layer_norm_strided_rows():
+    """Rows with a stride above n (a view of wider rows) are read in place."""
+    from spatten_b200.proj import add_layer_norm
+    g = torch.Generator().manual_seed(5)
+    wide = torch.randn(64, 1024, generator=g).half().cuda()
+    x = wide[:, :768]
+    w = torch.ones(768, dtype=torch.float16, device="cuda")
+    b = torch.zeros(768, dtype=torch.float16, device="cuda")
+    got = add_layer_norm(x, w, b, 1e-12)
+    ref = torch.nn.functional.layer_norm(x, (768,), w, b, 1e-12)
+    torch.testing.assert_close(got.float(), ref.float(), rtol=RTOL[torch.float16], atol=RTOL[torch.float16])
