@@ -884,7 +884,7 @@ def ours_arm(args, torch, rank, world, local_rank):
 
 
 MICRO_KERNELS = ("quant_q", "quant_k", "topk_decode", "topk_cascade", "gather", "op", "compat",
-                 "f32", "qk_norm_rope", "qkv_proj", "out_proj")
+                 "f32", "qk_norm_rope", "qkv_proj", "out_proj", "layer_norm")
 
 
 def micro_bench(torch, dev, name, steps):
@@ -977,6 +977,14 @@ def micro_bench(torch, dev, name, steps):
         fn = lambda: compact_out_proj(ctx, res, kept, w, bias, 12, 64, heads=heads)  # noqa: E731
         info = dict(case="BERT output projection on the kept rows, 32 x 461 of 512 rows, 768 -> 768, "
                          "bias + gathered residual", flops=2 * 32 * 461 * 768 * 768)
+    elif name == "layer_norm":
+        from spatten_b200.proj import add_layer_norm
+        x = rn(32 * 461, 768)
+        res = rn(32 * 461, 768)
+        w, b = 1 + 0.1 * rn(768), 0.1 * rn(768)
+        fn = lambda: add_layer_norm(x, w, b, 1e-12, residual=res)  # noqa: E731
+        info = dict(case="BERT-base residual add + LayerNorm, 32 x 461 rows x 768 fp16",
+                    bytes=3 * x.numel() * 2 + 2 * 768 * 2)
     else:
         raise ValueError(f"--micro {name}: one of {', '.join(MICRO_KERNELS)}")
     for _ in range(3):

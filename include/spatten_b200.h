@@ -41,6 +41,9 @@
  *   spatten_add_layer_norm
  *       the residual add + LayerNorm of the HF BertLayer tail that the
  *       reference's encoder loop runs per layer (module.py:75).
+ *   spatten_select_heads
+ *       the head decision of the cascade: head importance, top-k and the
+ *       next layer's active heads (spatten_bert.py:120-128, module.py:89).
  */
 #ifndef SPATTEN_B200_H
 #define SPATTEN_B200_H
@@ -390,6 +393,20 @@ int spatten_gather_rows(const void* src, int64_t src_b_stride, int64_t src_r_str
 int spatten_add_layer_norm(const void* x, int64_t x_row_stride, const void* res, int64_t res_row_stride,
                            const void* gamma, const void* beta, void* y, int64_t y_row_stride,
                            int64_t rows, int n, int dtype, float eps, void* stream);
+
+/*
+ * Head decision of one cascade layer, one launch:
+ *   importance_out[i] = importance[i] * scale            (i < cur; optional, may be `importance`)
+ *   pos = ascending positions of the `keep` largest importance_out values
+ *         (ties at the k-th value to the smaller position, as spatten_topk_indices)
+ *   next_heads[j] = heads ? heads[pos[j]] : pos[j]       (int64 [keep])
+ *   next_heads32[j] = the same as int32                  (optional)
+ * Replaces `head_importance / count`, torch.topk + sort and the index of the
+ * active head list (spatten_bert.py:120-128, module.py:89). 1 <= keep <= cur
+ * <= 1024; all pointers on the device.
+ */
+int spatten_select_heads(const float* importance, float scale, const int64_t* heads, int cur, int keep,
+                         float* importance_out, int64_t* next_heads, int32_t* next_heads32, void* stream);
 
 #ifdef __cplusplus
 }

@@ -115,6 +115,7 @@ SIGNATURES = {
                                     c_i64, c_i64, c_vp, c_i64, c_i64, c_vp]),
     "spatten_add_layer_norm": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_int,
                                        c_int, ctypes.c_float, c_vp]),
+    "spatten_select_heads": (c_int, [c_vp, ctypes.c_float, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
 }
 
 

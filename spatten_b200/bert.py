@@ -49,7 +49,7 @@ from transformers.pytorch_utils import apply_chunking_to_forward
 from . import _native as N
 from .progressive import prog_attn, quant_k_planes, quant_q_int8
 from .proj import LAYER_NORM_FEATURES, add_layer_norm, compact_out_proj, qkv_proj
-from .select import gather_head_rows, gather_rows, topk_indices
+from .select import gather_head_rows, gather_rows, select_heads, topk_indices
 
 
 def keep_count(ratio, current):
@@ -101,6 +101,7 @@ class SpattenBertSelfAttention(BertSelfAttention):
         self.head_prune_num = 0
         self.enable_head_prune = False
         self.next_active_head_indices = None
+        self.next_active_head_indices32 = None  # int32 copy (the next layer's head-slot map)
         self.active_head_indices_for_this_layer = None
         self.enable_token_prune = False
         self.token_prune_num = 0
@@ -155,6 +156,10 @@ class SpattenBertSelfAttention(BertSelfAttention):
         if heads is None:
             heads = torch.arange(H, device=dev)
         cur = heads.numel()
+        # the int32 copy of `heads` that the encoder loop handed over with it
+        # (the attention kernel's head-slot map); else prog_attn converts
+        h32 = getattr(self, "_heads32", None)
+        head_map = h32[1] if (h32 is not None and h32[0] is heads) else heads
         w, b = self._qkv_params()
         fused = hidden_states.dtype in (torch.float16, torch.bfloat16) and d in (64, 128)
         if fused:
@@ -193,7 +198,7 @@ class SpattenBertSelfAttention(BertSelfAttention):
         common = dict(sm_scale=1.0 / math.sqrt(d), v_thr=v_thr, v_prune_count=v_count, bias=bias,
                       tok_in=cum,
                       want_tok=True, want_head=True, out=full.permute(0, 2, 1, 3),
-                      out_head_map=heads, out_head_slots=H)
+                      out_head_map=head_map, out_head_slots=H)
         if self.enable_prog_quant:
             if fused:
                 q8, qs, kp = pr.q8, pr.q_scale, pr.k_planes
@@ -210,17 +215,22 @@ class SpattenBertSelfAttention(BertSelfAttention):
             r = prog_attn(q, k, v, mode=N.MODE_DENSE, **common)
         if self.process_group is not None:
             from .distributed import allreduce_head_importance
-            head_imp = allreduce_head_importance(r.head_abs_sum, B * S * d, self.process_group)
+            head_raw = allreduce_head_importance(r.head_abs_sum, B * S * d, self.process_group)
+            scale = 1.0
         else:
-            head_imp = r.head_abs_sum / float(B * S * d)
-        self.last_head_importance = head_imp
+            head_raw, scale = r.head_abs_sum, 1.0 / float(B * S * d)
         hp, tp = self._prune_counts(cur, S)
-        next_heads = heads
+        next_heads, next32 = heads, head_map
         if self.enable_head_prune and cur > hp:
             keep = max(1, cur - hp)
-            pos = topk_indices(head_imp, keep)
-            next_heads = heads[pos]
+            # importance, top-k and heads[pos] in one launch, with the int32
+            # copy of the next heads that the next layer's head-slot map reads
+            head_imp, next_heads, next32 = select_heads(head_raw, scale, heads, keep)
+        else:
+            head_imp = head_raw * scale if scale != 1.0 else head_raw
+        self.last_head_importance = head_imp
         self.next_active_head_indices = next_heads
+        self.next_active_head_indices32 = next32
         self.cumulative_token_score = r.token_importance
         next_tokens = None
         if self.enable_token_prune and S > tp:
@@ -293,6 +303,7 @@ def spatten_encoder_forward(self, hidden_states, attention_mask=None, **kwargs):
     are not gathered again (``compact_ffn = False`` on the attention module
     turns this off)."""
     active_heads = None
+    active_heads32 = None
     active_tokens = None
     cumulative = None
     compacted = False
@@ -319,6 +330,7 @@ def spatten_encoder_forward(self, hidden_states, attention_mask=None, **kwargs):
                 cumulative = gather_rows(cumulative, active_tokens)
         attn = layer.attention.self
         attn.active_head_indices_for_this_layer = active_heads
+        attn._heads32 = (active_heads, active_heads32) if active_heads is not None else None
         attn.cumulative_token_score = cumulative
         if _compactable(layer, attn, hidden_states, last=(i == n_layers - 1)):
             ctx, _ = attn(hidden_states, attention_mask=attention_mask, **kwargs)
@@ -330,6 +342,7 @@ def spatten_encoder_forward(self, hidden_states, attention_mask=None, **kwargs):
             hidden_states = out[0] if isinstance(out, (tuple, list)) else out
             compacted = False
         active_heads = attn.next_active_head_indices
+        active_heads32 = getattr(attn, "next_active_head_indices32", None)
         active_tokens = attn.next_active_token_indices
         cumulative = attn.cumulative_token_score
     return BaseModelOutputWithPastAndCrossAttentions(

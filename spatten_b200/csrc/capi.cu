@@ -263,6 +263,17 @@ int spatten_gather_rows(const void* src, int64_t src_b_stride, int64_t src_r_str
                      "gather launch");
 }
 
+int spatten_select_heads(const float* importance, float scale, const int64_t* heads, int cur, int keep,
+                         float* importance_out, int64_t* next_heads, int32_t* next_heads32, void* stream) {
+  if (!importance || !next_heads) return fail(SPATTEN_ERR_INVALID, "select_heads: null pointer");
+  if (cur < 1 || cur > 1024) return fail(SPATTEN_ERR_UNSUPPORTED, "select_heads: cur=%d (need 1..1024)", cur);
+  if (keep < 1 || keep > cur) return fail(SPATTEN_ERR_INVALID, "select_heads: keep=%d (need 1..%d)", keep, cur);
+  if (!(scale == scale)) return fail(SPATTEN_ERR_INVALID, "select_heads: scale is NaN");
+  return cuda_status(spatten::launch_select_heads(importance, scale, heads, cur, keep, importance_out, next_heads,
+                                                  next_heads32, (cudaStream_t)stream),
+                     "select_heads launch");
+}
+
 int spatten_add_layer_norm(const void* x, int64_t x_row_stride, const void* res, int64_t res_row_stride,
                            const void* gamma, const void* beta, void* y, int64_t y_row_stride,
                            int64_t rows, int n, int dtype, float eps, void* stream) {

@@ -74,6 +74,10 @@ cudaError_t launch_gather(const void* src, int64_t src_b, int64_t src_r, const i
                           int64_t row_bytes, void* dst, int64_t dst_b, int64_t dst_r,
                           cudaStream_t st, int n_sm, int64_t src_rows);
 
+// Head importance scaling + top-k + next active heads (heads.cu); cur <= 1024.
+cudaError_t launch_select_heads(const float* imp_in, float scale, const int64_t* heads, int cur, int keep,
+                                float* imp_out, int64_t* next_heads, int32_t* next_heads32, cudaStream_t st);
+
 // Residual add + LayerNorm over rows of n features (layernorm.cu).
 bool add_layer_norm_supported(int n);
 cudaError_t launch_add_layer_norm(const void* x, const void* res, const void* gamma, const void* beta,

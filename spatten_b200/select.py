@@ -79,3 +79,29 @@ def gather_head_rows(w, heads, head_dim):
         s3 = s3.contiguous()
     out = _gather(s3, heads.reshape(1, -1), head_dim, head_dim, True)
     return out.reshape((heads.numel() * head_dim,) + tuple(tail))
+
+
+def select_heads(importance, scale, heads, keep):
+    """Head decision of a cascade layer in one launch (spatten_select_heads):
+    the importance scaled by ``scale`` (fp32 [cur]), the ``keep`` most
+    important positions in ascending order (ties to the smaller position, as
+    ``topk_indices``) and those positions mapped through ``heads`` (int64
+    [cur] active heads, or None for 0..cur-1). Returns (scaled importance,
+    next heads int64 [keep], next heads int32 [keep])."""
+    if not importance.is_cuda:
+        raise ValueError("select_heads takes CUDA tensors; there is no CPU path")
+    imp = importance.reshape(-1)
+    if imp.dtype != torch.float32 or not imp.is_contiguous():
+        imp = imp.float().contiguous()
+    cur = imp.numel()
+    if heads is not None:
+        heads = heads.to(torch.int64).contiguous()
+        if heads.numel() != cur:
+            raise ValueError(f"select_heads: {heads.numel()} heads for {cur} importance values")
+    out = torch.empty(cur, dtype=torch.float32, device=imp.device)
+    nxt = torch.empty(keep, dtype=torch.int64, device=imp.device)
+    nxt32 = torch.empty(keep, dtype=torch.int32, device=imp.device)
+    N.check(N.lib.spatten_select_heads(imp.data_ptr(), float(scale), None if heads is None else heads.data_ptr(),
+                                       cur, int(keep), out.data_ptr(), nxt.data_ptr(), nxt32.data_ptr(),
+                                       _stream(imp)))
+    return out, nxt, nxt32

@@ -267,3 +267,18 @@ def test_add_layer_norm_args_validation():
     assert f(p, 768, None, 0, p, p, p, 768, 10, 768, N.DTYPE_F16, -1.0, None) == N.ERR_INVALID  # eps
     assert f(p, 768, None, 0, p, p, p, 768, -1, 768, N.DTYPE_F16, 1e-12, None) == N.ERR_INVALID
     assert f(None, 0, None, 0, None, None, None, 0, 0, 768, N.DTYPE_F16, 1e-12, None) == N.OK
+
+
+def test_select_heads_args_validation():
+    """The head decision rejects bad sizes before any launch."""
+    from spatten_b200 import _native as N
+    f = N.lib.spatten_select_heads
+    p = 1 << 20
+    # importance, scale, heads, cur, keep, importance_out, next_heads, next_heads32, stream
+    assert f(None, 1.0, None, 12, 10, None, p, None, None) == N.ERR_INVALID
+    assert f(p, 1.0, None, 12, 10, None, None, None, None) == N.ERR_INVALID
+    assert f(p, 1.0, None, 0, 1, None, p, None, None) == N.ERR_UNSUPPORTED
+    assert f(p, 1.0, None, 1025, 1, None, p, None, None) == N.ERR_UNSUPPORTED
+    assert f(p, 1.0, None, 12, 0, None, p, None, None) == N.ERR_INVALID
+    assert f(p, 1.0, None, 12, 13, None, p, None, None) == N.ERR_INVALID
+    assert f(p, float("nan"), None, 12, 10, None, p, None, None) == N.ERR_INVALID
