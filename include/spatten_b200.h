@@ -58,7 +58,7 @@ extern "C" {
 #define SPATTEN_OK 0
 #define SPATTEN_ERR_INVALID 1     /* bad argument (shape, stride, pointer, dtype) */
 #define SPATTEN_ERR_CUDA 2        /* a CUDA runtime call or launch failed */
-#define SPATTEN_ERR_UNSUPPORTED 3 /* valid request outside what this build implements */
+#define SPATTEN_ERR_UNSUPPORTED 3 /* valid request outside what this library implements */
 
 #define SPATTEN_DTYPE_F16 0
 #define SPATTEN_DTYPE_BF16 1

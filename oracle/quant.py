@@ -4,7 +4,7 @@ Test infrastructure only (see ``oracle/__init__.py``).
 
 The reference splits K into two *float* planes, ``k_msb = 0.8*K`` and
 ``k_lsb = 0.2*K`` (spatten_bert_ultimate.py:184-185). The progressive
-quantisation asked of this build uses real integer planes instead:
+quantisation of this library uses real integer planes instead:
 
 * ``scale = max_d |x| / 127``  (fp32 division)
 * ``x8 = clamp(rint(x / scale), -127, 127)``  (fp32 division, round half to
