@@ -296,7 +296,7 @@ int spatten_add_layer_norm(const void* x, int64_t x_row_stride, const void* res,
       !a16(gamma, 0) || !a16(beta, 0))
     return fail(SPATTEN_ERR_INVALID, "add_layer_norm: rows, gamma and beta must start on 16-byte boundaries");
   return cuda_status(spatten::launch_add_layer_norm(x, res, gamma, beta, y, rows, n, x_row_stride,
-                                                    res_row_stride, y_row_stride, dtype, eps,
+                                                    res_row_stride, y_row_stride, dtype, eps, sm_count(),
                                                     (cudaStream_t)stream),
                      "add_layer_norm launch");
 }

@@ -82,7 +82,7 @@ cudaError_t launch_select_heads(const float* imp_in, float scale, const int64_t*
 bool add_layer_norm_supported(int n);
 cudaError_t launch_add_layer_norm(const void* x, const void* res, const void* gamma, const void* beta,
                                   void* y, int64_t rows, int n, int64_t xs, int64_t rs, int64_t ys,
-                                  int dtype, float eps, cudaStream_t st);
+                                  int dtype, float eps, int n_sm, cudaStream_t st);
 
 // Per-head RMSNorm + rotary embedding of Q and K, Q quantised (qk_prep.cu).
 struct QkPrepParams {
