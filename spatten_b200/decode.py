@@ -100,17 +100,28 @@ def decode_attend(q, cache, kept, sm_scale=None, n_valid=None, q_quant=None):
     return out
 
 
-def decode_attention(q, cache, top_k=2048, sm_scale=None, n_valid=None, process_group=None):
+def decode_attention(q, cache, top_k=2048, sm_scale=None, n_valid=None, process_group=None,
+                     split_batch=False):
     """One decode step: importance, (all-reduce,) top-k, attention over the
     kept keys. ``q`` [B, H_local, D]; with ``process_group`` the cache holds
-    this rank's KV heads and the importance is summed over all ranks' heads."""
+    this rank's KV heads and the importance is summed over all ranks' heads.
+    With ``split_batch`` (and B a multiple of the group size) the sum and the
+    selection are split over the batch instead (reduce-scatter, top-k of the
+    rank's rows, all-gather of the kept indices: ``topk_by_batch_shard``);
+    every rank still gets all B rows of kept keys, and ``importance`` of the
+    result is then this rank's B / world summed rows."""
     qq = _quant_query(q)
     imp = decode_importance(q, cache, sm_scale, n_valid, q_quant=qq)
+    nv = cache.planes.msb.shape[2] if n_valid is None else int(n_valid)
+    k = min(int(top_k), nv)
+    if process_group is not None and split_batch:
+        from .distributed import topk_by_batch_shard
+        kept, imp = topk_by_batch_shard(imp[:, :nv], k, process_group)
+        out = decode_attend(q, cache, kept, sm_scale, n_valid, q_quant=qq)
+        return DecodeResult(out, kept, imp)
     if process_group is not None:
         import torch.distributed as dist
         dist.all_reduce(imp, op=dist.ReduceOp.SUM, group=process_group)
-    nv = cache.planes.msb.shape[2] if n_valid is None else int(n_valid)
-    k = min(int(top_k), nv)
     kept = topk_indices(imp[:, :nv], k)
     out = decode_attend(q, cache, kept, sm_scale, n_valid, q_quant=qq)
     return DecodeResult(out, kept, imp)

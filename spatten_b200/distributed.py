@@ -105,3 +105,28 @@ class HeadBatchShards:
     def take(self, x):
         """This rank's units of a [B, H, ...] tensor."""
         return x[self.b0:self.b1, self.h0:self.h1]
+
+
+def topk_by_batch_shard(importance, k, group=None, topk=None):
+    """Token top-k of a summed importance [B, N] whose per-rank partial sums
+    each rank holds (KV heads split over ranks), with the selection itself
+    split over the batch: a reduce-scatter leaves each rank the summed rows
+    of its B / world batch rows, the rank takes their top-k, and an
+    all-gather of the kept indices gives every rank all B rows. Moves
+    (world - 1) / world of the importance once instead of twice, and each
+    rank selects B / world rows instead of B. B must be a multiple of the
+    group size. ``topk(x, k)`` -> int64 [rows, k] ascending indices (the
+    CUDA top-k by default). Returns (kept int64 [B, k], this rank's summed
+    importance rows [B / world, N])."""
+    if topk is None:
+        from .select import topk_indices as topk
+    w = dist.get_world_size(group)
+    B, n = importance.shape
+    if B % w:
+        raise ValueError(f"topk_by_batch_shard: batch {B} is not a multiple of the {w} ranks")
+    part = torch.empty((B // w, n), dtype=importance.dtype, device=importance.device)
+    dist.reduce_scatter_tensor(part, importance.contiguous(), op=dist.ReduceOp.SUM, group=group)
+    kept_part = topk(part, k).contiguous()
+    kept = torch.empty((B, k), dtype=kept_part.dtype, device=kept_part.device)
+    dist.all_gather_into_tensor(kept, kept_part, group=group)
+    return kept, part

@@ -120,3 +120,48 @@ def test_gloo_four_ranks_head_group_allreduce():
     full = x.sum(dim=1).numpy()
     for rank, b0, b1, tok in out:
         np.testing.assert_allclose(tok, full[b0:b1], rtol=1e-6)
+
+
+def _cpu_topk(x, k):
+    """Ascending indices of the k largest, ties to the smaller index (the
+    order spatten_topk_indices gives)."""
+    idx = torch.argsort(-x, dim=1, stable=True)[:, :k]
+    return torch.sort(idx, dim=1).values
+
+
+def _batch_split_worker(rank, world, port, parts, k, q):
+    import torch.distributed as dist
+    from spatten_b200 import distributed as sd
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        kept, mine = sd.topk_by_batch_shard(parts[rank].clone(), k, topk=_cpu_topk)
+        q.put((rank, kept.numpy(), mine.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_two_ranks_decode_topk_by_batch_shard():
+    """The decode selection split over the batch (reduce-scatter of the
+    per-rank importance, top-k of each rank's rows, all-gather of the kept
+    indices) gives every rank the kept keys of the summed importance of all
+    batch rows, as one process selecting on the full sum."""
+    g = torch.Generator().manual_seed(3)
+    world, B, n, k = 2, 6, 40, 9
+    parts = [torch.round(torch.rand(B, n, generator=g) * 8) / 8 for _ in range(world)]  # with ties
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    port = _free_port()
+    procs = [mpc.Process(target=_batch_split_worker, args=(r, world, port, parts, k, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    total = parts[0] + parts[1]
+    ref = _cpu_topk(total, k).numpy()
+    for rank, kept, mine in out:
+        assert np.array_equal(kept, ref), rank
+        np.testing.assert_allclose(mine, total[rank * B // world:(rank + 1) * B // world].numpy(), rtol=0)
