@@ -546,8 +546,7 @@ def decode_bench(torch, rank, world, dev, steps=3, batch=DEC_B):
     head_dim 128, 36 layers), bf16, batch 64, a KV cache of 32768 tokens with
     K / V drawn N(0,1) from seed 0, K as 4-bit MSB / LSB planes, top-k keeps
     2048 tokens per step. The KV heads are split over the ranks; the token
-    importance is reduce-scattered over the batch rows, each rank selects the
-    top-k of its rows and the kept indices are all-gathered. One layer's cache (6.5 GB at
+    importance is all-reduced before the top-k. One layer's cache (6.5 GB at
     one rank) serves all 36 layers' calls: every layer does the same work on
     the same amount of memory. ms per decode step (36 layers), tokens/s
     (batch / step) and the HBM roofline of one layer."""
@@ -562,7 +561,9 @@ def decode_bench(torch, rank, world, dev, steps=3, batch=DEC_B):
     qs = [torch.randn(batch, H, DEC_D, generator=g, device=dev, dtype=torch.bfloat16)
           for _ in range(DEC_LAYERS)]
     grp = dist.group.WORLD if world > 1 else None
-    split = world > 1 and batch % world == 0
+    # the importance is all-reduced (decode_attention's split_batch mode, a
+    # reduce-scatter + per-rank top-k + all-gather, is the alternative)
+    split = False
 
     def step():
         out = None
@@ -586,8 +587,7 @@ def decode_bench(torch, rank, world, dev, steps=3, batch=DEC_B):
             "batch": batch, "cache_len": DEC_N, "top_k": DEC_TOPK, "layers": DEC_LAYERS,
             "kv_heads_per_gpu": G, "dtype": "bf16",
             "config": "Qwen3-8B decode attention: 32 Q / 8 KV heads, head_dim 128, K/V N(0,1), K as "
-                      "4-bit planes, importance summed over KV-head shards (reduce-scatter over the batch, "
-                      "per-rank top-k, all-gather of the kept keys), top-2048 per step"}
+                      "4-bit planes, importance all-reduced over KV-head shards, top-2048 per step"}
 
 
 class OpRunner:
